@@ -1,0 +1,190 @@
+// Harness around Marco-Christiani/pkt's OWN megakernel, compiled from the
+// reference headers where they lie (include path given by oracle/Makefile).
+//
+// TEST INFRASTRUCTURE ONLY: built into oracle/_ref/libpkt_ref.so and loaded by
+// the GPU parity tests as the second opinion (pkt's CUDA kernel on identical
+// seeded inputs). The product library never links or calls it.
+//
+// Every entry point validates pkt's documented domain on the host before it
+// launches anything, so pkt's debug traps (include/ops/linear_fwd.cuh:201-212,
+// include/ops/linear_bwd.cuh:38-49) are never reached:
+//   LinearForward: tile_m_count == 2, n <= 1024
+//   LinearBackward: batch <= 64, tile_m_count <= 64
+// Returns 0 on success, a negative code when the case is outside pkt's domain
+// or a CUDA call failed.
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "include/ops/axpy.cuh"
+#include "include/ops/linear_bwd.cuh"
+#include "include/ops/linear_fwd.cuh"
+#include "include/ops/mse.cuh"
+#include "include/ops/sgd.cuh"
+#include "include/ops/zero.cuh"
+#include "include/runtime.hpp"
+
+namespace {
+
+#define HCHECK(x)                        \
+  do {                                   \
+    if ((x) != cudaSuccess) return -100; \
+  } while (0)
+
+}  // namespace
+
+extern "C" {
+
+int pktref_device_count() {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+// pkt Axpy tasks: num_tasks tasks of `per_task` elements each over x/y
+// (host arrays of num_tasks*per_task floats); y updated in place.
+int pktref_axpy(const float* hx, float* hy, float a, int num_tasks, int per_task, int blocks) {
+  const size_t n = size_t(num_tasks) * per_task;
+  float *dx = nullptr, *dy = nullptr;
+  HCHECK(cudaMalloc(&dx, n * 4));
+  HCHECK(cudaMalloc(&dy, n * 4));
+  HCHECK(cudaMemcpy(dx, hx, n * 4, cudaMemcpyHostToDevice));
+  HCHECK(cudaMemcpy(dy, hy, n * 4, cudaMemcpyHostToDevice));
+  {
+    pk::Runtime rt;
+    rt.initialize(num_tasks);
+    std::vector<pk::Task> tasks(num_tasks);
+    for (int i = 0; i < num_tasks; ++i) {
+      pk::AxpyArgs args{dx + size_t(i) * per_task, dy + size_t(i) * per_task, a, per_task};
+      pk::encode_args(tasks[i], pk::OpCode::Axpy, args);
+    }
+    rt.submit_tasks(tasks);
+    rt.launch(blocks > 0 ? blocks : pk::Runtime::get_num_sms());
+    rt.synchronize();
+  }
+  HCHECK(cudaGetLastError());
+  HCHECK(cudaMemcpy(hy, dy, n * 4, cudaMemcpyDeviceToHost));
+  cudaFree(dx);
+  cudaFree(dy);
+  return 0;
+}
+
+// pkt's single-Linear training DAG (same task structure as the train_linear
+// example: zero loss, forward tiles, MSE, zero dW, backward tiles, SGD), all
+// steps in one launch, but each step's MSELossArgs.loss points at its own slot
+// so the whole loss curve comes back. W updated in place (host array).
+int pktref_train_linear(float* hW, const float* hx, const float* ht, int batch, int m, int n,
+                        int steps, float lr, float* losses, int blocks) {
+  const int fwd_tm = 2, fwd_tn = 128, bwd_tm = 64, bwd_tn = 128;
+  if (n > 1024 || batch > 64 || batch <= 0 || m <= 0 || n <= 0 || steps <= 0) return -1;
+  float *dW, *dx, *dy, *dt, *ddy, *ddW, *dloss;
+  HCHECK(cudaMalloc(&dW, size_t(m) * n * 4));
+  HCHECK(cudaMalloc(&dx, size_t(batch) * n * 4));
+  HCHECK(cudaMalloc(&dy, size_t(batch) * m * 4));
+  HCHECK(cudaMalloc(&dt, size_t(batch) * m * 4));
+  HCHECK(cudaMalloc(&ddy, size_t(batch) * m * 4));
+  HCHECK(cudaMalloc(&ddW, size_t(m) * n * 4));
+  HCHECK(cudaMalloc(&dloss, size_t(steps) * 4));
+  HCHECK(cudaMemcpy(dW, hW, size_t(m) * n * 4, cudaMemcpyHostToDevice));
+  HCHECK(cudaMemcpy(dx, hx, size_t(batch) * n * 4, cudaMemcpyHostToDevice));
+  HCHECK(cudaMemcpy(dt, ht, size_t(batch) * m * 4, cudaMemcpyHostToDevice));
+  HCHECK(cudaMemset(dloss, 0, size_t(steps) * 4));
+
+  const uint16_t kLoss = 1, kGrad = 2, kDW = 3, kW = 4;
+  std::vector<pk::Task> tasks;
+  int r_loss = 0, r_grad = 0, r_dw = 0, r_w = 0, e_grad = 0, e_dw = 0, e_w = 0;
+  const int ftm = (batch + fwd_tm - 1) / fwd_tm, ftn = (m + fwd_tn - 1) / fwd_tn;
+  const int btm = (m + bwd_tm - 1) / bwd_tm, btn = (n + bwd_tn - 1) / bwd_tn;
+  for (int s = 0; s < steps; ++s) {
+    const int ep = s + 1;
+    pk::Task t{};
+    pk::ZeroMemoryArgs z{dloss + s, 1};
+    pk::encode_args(t, pk::OpCode::ZeroMemory, z);
+    t.header.buffer_write_id = kLoss;
+    t.header.write_epoch = ep;
+    tasks.push_back(t);
+    r_loss++;
+    for (int tm = 0; tm < ftm; ++tm) {
+      const int ms = tm * fwd_tm, mc = (ms + fwd_tm <= batch) ? fwd_tm : batch - ms;
+      if (mc != fwd_tm) return -2;  // pkt requires full 2-row tiles (linear_fwd.cuh:201-205)
+      for (int tn = 0; tn < ftn; ++tn) {
+        const int ns = tn * fwd_tn, nc = (ns + fwd_tn <= m) ? fwd_tn : m - ns;
+        pk::Task f{};
+        pk::LinearForwardArgs a{dW, dx, dy, batch, m, n, ms, mc, ns, nc};
+        pk::encode_args(f, pk::OpCode::LinearForward, a);
+        f.header.buffer_read_id = kW;
+        f.header.buffer_write_id = kLoss;
+        f.header.wait_count = r_w;
+        f.header.read_epoch = e_w;
+        f.header.write_epoch = ep;
+        tasks.push_back(f);
+        r_loss++;
+      }
+    }
+    pk::Task l{};
+    pk::MSELossArgs la{dy, dt, ddy, dloss + s, batch, m};
+    pk::encode_args(l, pk::OpCode::MSELoss, la);
+    l.header.buffer_read_id = kLoss;
+    l.header.buffer_write_id = kGrad;
+    l.header.wait_count = r_loss;
+    l.header.read_epoch = ep;
+    l.header.write_epoch = ++e_grad;
+    tasks.push_back(l);
+    r_grad++;
+    pk::Task zd{};
+    pk::ZeroMemoryArgs zda{ddW, m * n};
+    pk::encode_args(zd, pk::OpCode::ZeroMemory, zda);
+    zd.header.buffer_write_id = kGrad;
+    zd.header.write_epoch = ++e_grad;
+    tasks.push_back(zd);
+    r_grad++;
+    for (int tm = 0; tm < btm; ++tm) {
+      const int ms = tm * bwd_tm, mc = (ms + bwd_tm <= m) ? bwd_tm : m - ms;
+      for (int tn = 0; tn < btn; ++tn) {
+        const int ns = tn * bwd_tn, nc = (ns + bwd_tn <= n) ? bwd_tn : n - ns;
+        pk::Task bt{};
+        pk::LinearBackwardArgs ba{ddy, dx, ddW, batch, m, n, ms, mc, ns, nc};
+        pk::encode_args(bt, pk::OpCode::LinearBackward, ba);
+        bt.header.buffer_read_id = kGrad;
+        bt.header.buffer_write_id = kDW;
+        bt.header.wait_count = r_grad;
+        bt.header.read_epoch = e_grad;
+        bt.header.write_epoch = ++e_dw;
+        tasks.push_back(bt);
+        r_dw++;
+      }
+    }
+    pk::Task sg{};
+    pk::SGDUpdateArgs sa{dW, ddW, lr, m * n};
+    pk::encode_args(sg, pk::OpCode::SGDUpdate, sa);
+    sg.header.buffer_read_id = kDW;
+    sg.header.buffer_write_id = kW;
+    sg.header.wait_count = r_dw;
+    sg.header.read_epoch = e_dw;
+    sg.header.write_epoch = ++e_w;
+    tasks.push_back(sg);
+    r_w++;
+  }
+  {
+    pk::Runtime rt;
+    rt.initialize(int(tasks.size()));
+    rt.submit_tasks(tasks);
+    rt.launch(blocks > 0 ? blocks : pk::Runtime::get_num_sms());
+    rt.synchronize();
+  }
+  HCHECK(cudaGetLastError());
+  HCHECK(cudaMemcpy(hW, dW, size_t(m) * n * 4, cudaMemcpyDeviceToHost));
+  HCHECK(cudaMemcpy(losses, dloss, size_t(steps) * 4, cudaMemcpyDeviceToHost));
+  cudaFree(dW);
+  cudaFree(dx);
+  cudaFree(dy);
+  cudaFree(dt);
+  cudaFree(ddy);
+  cudaFree(ddW);
+  cudaFree(dloss);
+  return 0;
+}
+
+}  // extern "C"
