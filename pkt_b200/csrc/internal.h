@@ -1,0 +1,134 @@
+// Definitions shared by the host runtime and the device megakernel.
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+#include "../../include/pkt_b200.h"
+
+namespace pkb {
+
+// pkt's argument structs (include/ops/*.cuh), byte-identical.
+struct ZeroMemoryArgs {  // include/ops/zero.cuh:10-13
+  float* ptr;
+  int size;
+};
+struct AxpyArgs {  // include/ops/axpy.cuh:9-15
+  const float* x;
+  float* y;
+  float a;
+  int n;
+};
+struct LinearForwardArgs {  // include/ops/linear_fwd.cuh:18-29
+  const float* W;
+  const float* x;
+  float* y;
+  int batch, m, n, tile_m_start, tile_m_count, tile_n_start, tile_n_count;
+};
+struct LinearBackwardArgs {  // include/ops/linear_bwd.cuh:16-27
+  const float* dy;
+  const float* x;
+  float* dW;
+  int batch, m, n, tile_m_start, tile_m_count, tile_n_start, tile_n_count;
+};
+struct MSELossArgs {  // include/ops/mse.cuh:13-20
+  const float* y;
+  const float* target;
+  float* dy;
+  float* loss;
+  int batch, m;
+};
+struct SGDUpdateArgs {  // include/ops/sgd.cuh:12-17
+  float* W;
+  const float* dW;
+  float lr;
+  int size;
+};
+static_assert(sizeof(ZeroMemoryArgs) == 16, "pkt ZeroMemoryArgs layout");
+static_assert(sizeof(AxpyArgs) == 24, "pkt AxpyArgs layout");
+static_assert(sizeof(LinearForwardArgs) == 56, "pkt LinearForwardArgs layout");
+static_assert(sizeof(LinearBackwardArgs) == 56, "pkt LinearBackwardArgs layout");
+static_assert(sizeof(MSELossArgs) == 40, "pkt MSELossArgs layout");
+static_assert(sizeof(SGDUpdateArgs) == 24, "pkt SGDUpdateArgs layout");
+static_assert(sizeof(pkt_task) == 96, "pkt Task is 96 bytes");
+static_assert(sizeof(pkt_task_header) == 32, "pkt TaskHeader is 32 bytes");
+static_assert(sizeof(pkt_bias_sgd_args) <= 64 && sizeof(pkt_sgd_mixed_args) <= 64 &&
+                  sizeof(pkt_loss_reduce_args) <= 64 && sizeof(pkt_gemm_tile_args) <= 64,
+              "args fit the 64-byte payload");
+
+// CTA shape of the megakernel (pkt's warp numbering, include/config.cuh:17-27):
+//   warp 0 controller  : dequeues tasks, waits on dependency tokens, fills the slot ring
+//   warp 1 loader      : TMA tile loads into the shared-memory stage ring
+//   warp 2 MMA issuer  : tcgen05.mma into the TMEM accumulators (pkt's "storer" index)
+//   warps 3-6 compute  : TMEM epilogues, SIMT ops, stores and token publication
+constexpr int kThreads = 224;
+constexpr int kCtrlWarp = 0;
+constexpr int kLoadWarp = 1;
+constexpr int kMmaWarp = 2;
+constexpr int kEpiWarp0 = 3;
+constexpr int kEpiThreads = 128;
+constexpr int kStages = 4;
+constexpr int kSlots = 4;
+constexpr int kBM = 128;
+constexpr int kMaxBN = 256;
+constexpr int kATileBytes = kBM * 128;
+constexpr int kBTileBytes = kMaxBN * 128;
+constexpr int kStageBytes = kATileBytes + kBTileBytes;
+constexpr int kTmemCols = 512;  // two 256-column fp32 accumulators
+constexpr uint16_t kOpStop = 0xFFFF;
+
+// Device copy of one registered GEMM.
+struct alignas(128) DevGemm {
+  CUtensorMap map_a;
+  CUtensorMap map_b;
+  pkt_gemm_desc d;
+  uint32_t idesc;
+  int tiles_m, tiles_n, num_kb, bk;
+  int a_boxes, b_boxes;    // TMA boxes per stage
+  int box_mn;              // elements per 128-byte row (MN-major box width)
+  uint32_t stage_tx;       // bytes landed per stage
+  uint32_t a_lbo, b_lbo;   // descriptor leading-byte offsets
+  uint32_t a_kstep, b_kstep;  // descriptor start advance per MMA (bytes)
+  uint32_t a_box_bytes, b_box_bytes;
+  uint32_t a_sbo, b_sbo;        // descriptor stride-byte offsets
+  uint32_t a_layout, b_layout;  // descriptor swizzle mode: 2 = 128B, 1 = 128B with 32B atoms
+  int mma_per_kb;
+  int pad_[3];
+};
+
+// Per-CTA perf words (pkt_runtime_fetch_perf), cycles unless noted.
+enum PerfWord {
+  kPerfTasks = 0,         // tasks executed (count)
+  kPerfGemmTiles = 1,     // GEMM tiles executed (count)
+  kPerfCtrlDepWait = 2,
+  kPerfCtrlSlotWait = 3,
+  kPerfLoadStageWait = 4,
+  kPerfMmaFullWait = 5,
+  kPerfMmaTmemWait = 6,
+  kPerfEpiTmemWait = 7,
+  kPerfEpiGemm = 8,
+  kPerfEpiSimt = 9,
+  kPerfTotal = 10,
+};
+
+struct KParams {
+  const pkt_task* tasks;
+  int num_tasks;
+  int num_tokens;
+  int* state;  // [0] cursor, [1..3] status code/task/detail, [4..] token counts, then epochs
+  const DevGemm* gemms;
+  int num_gemms;
+  int chunk;
+  unsigned long long* task_counter;
+  unsigned long long* perf;  // [gridDim.x][PKT_PERF_WORDS] or null
+  unsigned long long timeout_ns;
+};
+
+constexpr int kStateHeader = 8;  // ints before the token counters
+inline int state_ints(int num_tokens) { return kStateHeader + 2 * num_tokens; }
+
+// Launches the megakernel (megakernel.cu).
+cudaError_t launch_megakernel(const KParams& p, int blocks, cudaStream_t stream);
+int megakernel_smem_bytes();
+
+}  // namespace pkb

@@ -1,0 +1,947 @@
+// The persistent sm_100a megakernel: one CTA per SM pulls pkt tasks from a
+// device-resident queue and runs them through a warp-specialised pipeline.
+//
+// Replaces pkt's persistent_kernel (include/kernel.cuh:1351-1517) and its role
+// loops (controller :683-953, loader :956-1067, compute :1069-1205, storer
+// :1207-1341). What changed, B200-first:
+//   * intra-CTA handoff is mbarrier phase bits (slot ring + stage ring + TMEM
+//     accumulator ring), not polled smem atomics with nanosleep backoff
+//     (include/pipeline.cuh:40-47);
+//   * GEMM tiles (pkt's reserved OpCode::Gemm) run on tcgen05: TMA bulk-tensor
+//     loads (128B swizzle, no multicast) -> one elected thread issues
+//     tcgen05.mma into a double-buffered TMEM accumulator -> four warps read
+//     TMEM and apply the fused epilogue (bias+ReLU, MSE+dY, ReLU-masked dgrad,
+//     weight-gradient + SGD);
+//   * cross-CTA dependencies keep pkt's token semantics (cumulative count +
+//     max epoch, include/dependency.cuh:29-77) with ld.acquire / red.release,
+//     plus an optional second token per task (pkt's reserved header words);
+//   * every wait is bounded by a %globaltimer budget; on expiry the device
+//     writes a status word (code, task, detail) and every CTA drains, so a
+//     malformed DAG returns an error instead of hanging the GPU (pkt spins
+//     forever, include/kernel.cuh:873-881).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace pkb {
+
+namespace {
+
+struct Smem {
+  uint8_t stages[kStages][kStageBytes];  // 1024-byte aligned (kernel aligns the base)
+  pkt_task slots[kSlots];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t slot_full[kSlots];
+  uint64_t slot_empty[kSlots];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t mma_drain;
+  uint32_t tmem_base;
+  uint32_t pad0;
+  float red[8][4][32];  // per 32-column chunk, per TMEM lane quadrant: column partial sums
+  float lossred[4];
+  float simt_red[4];
+  double simt_redd[4];
+};
+
+constexpr int kSmemBytes = int(sizeof(Smem)) + 1024;
+
+__device__ __forceinline__ int* tok_count(const KParams& p) { return p.state + kStateHeader; }
+__device__ __forceinline__ int* tok_epoch(const KParams& p) {
+  return p.state + kStateHeader + p.num_tokens;
+}
+__device__ __forceinline__ volatile int* status_word(const KParams& p) {
+  return reinterpret_cast<volatile int*>(p.state + 1);
+}
+
+__device__ void set_error(const KParams& p, int code, int task, int detail) {
+  if (atomicCAS(p.state + 1, 0, code) == 0) {
+    p.state[2] = task;
+    p.state[3] = detail;
+    __threadfence();
+  }
+}
+
+// Bounded mbarrier wait. Returns false when the budget ran out or another
+// CTA reported an error while this one was waiting. `idle` waits (a consumer
+// waiting for the controller's next task, which may itself be waiting on a
+// dependency with the same budget) get four budgets plus one second, so the
+// controller's dependency timeout is the one reported.
+__device__ __forceinline__ bool wait_bar(const KParams& p, uint64_t* bar, uint32_t parity,
+                                         int where, bool idle = false) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  const uint64_t budget = idle ? 4 * p.timeout_ns + 1000000000ull : p.timeout_ns;
+  uint32_t it = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++it & 63u) == 0) {
+      if (*status_word(p) != 0) return false;
+      if (globaltimer_ns() - t0 > budget) {
+        set_error(p, PKT_DEV_TIMEOUT_PIPE, -1, where);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool opcode_known(uint16_t op) {
+  return op == PKT_OP_INVALID || op == PKT_OP_ZERO_MEMORY || op == PKT_OP_AXPY ||
+         op == PKT_OP_GEMM || op == PKT_OP_LINEAR_FORWARD || op == PKT_OP_MSE_LOSS ||
+         op == PKT_OP_LINEAR_BACKWARD || op == PKT_OP_SGD_UPDATE || op == PKT_OP_BIAS_SGD ||
+         op == PKT_OP_LOSS_REDUCE || op == PKT_OP_SGD_MIXED;
+}
+
+__device__ __forceinline__ void copy_task(pkt_task* dst, const pkt_task* src) {
+  const int4* s = reinterpret_cast<const int4*>(src);
+  int4* d = reinterpret_cast<int4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 6; ++i) d[i] = s[i];
+}
+
+// ============================================================ controller
+__device__ void controller_loop(const KParams& p, Smem& s, unsigned long long* perf) {
+  int seq = 0;
+  unsigned long long dep_cycles = 0, slot_cycles = 0, ntasks = 0;
+  int cursor_local = 0, cursor_end = 0;
+  while (true) {
+    if (*status_word(p) != 0) break;
+    if (cursor_local >= cursor_end) {
+      const int start = atomicAdd(p.state, p.chunk);
+      cursor_local = start;
+      cursor_end = min(start + p.chunk, p.num_tasks);
+      if (cursor_local >= cursor_end) break;
+    }
+    const int t = cursor_local++;
+    pkt_task task;
+    copy_task(&task, p.tasks + t);
+    const pkt_task_header& h = task.header;
+    if (!opcode_known(h.opcode)) {
+      set_error(p, PKT_DEV_BAD_OPCODE, t, h.opcode);
+      break;
+    }
+    const int r1 = h.buffer_read_id, r2 = int(h.ext_ids & 0xffffu);
+    const int w1 = h.buffer_write_id, w2 = int(h.ext_ids >> 16);
+    if (r1 >= p.num_tokens || r2 >= p.num_tokens || w1 >= p.num_tokens || w2 >= p.num_tokens) {
+      set_error(p, PKT_DEV_BAD_ARGS, t, -1);
+      break;
+    }
+    if (h.opcode == PKT_OP_GEMM) {
+      const pkt_gemm_tile_args* a = reinterpret_cast<const pkt_gemm_tile_args*>(task.args);
+      if (int(a->gemm) >= p.num_gemms || int(a->tile_m) >= p.gemms[a->gemm].tiles_m ||
+          int(a->tile_n) >= p.gemms[a->gemm].tiles_n) {
+        set_error(p, PKT_DEV_BAD_ARGS, t, -2);
+        break;
+      }
+    }
+    // ---- dependency wait (pkt semantics: count >= wait_count && epoch >= read_epoch)
+    if (r1 != 0 || r2 != 0) {
+      const long long c0 = clock64();
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t it = 0;
+      bool ok = true;
+      while (true) {
+        bool ready = true;
+        if (r1 != 0) {
+          ready = ld_acquire_gpu(tok_count(p) + r1) >= int(h.wait_count) &&
+                  ld_acquire_gpu(tok_epoch(p) + r1) >= int(h.read_epoch);
+        }
+        if (ready && r2 != 0) ready = ld_acquire_gpu(tok_count(p) + r2) >= int(h.ext_wait_count);
+        if (ready) break;
+        if ((++it & 15u) == 0) {
+          if (*status_word(p) != 0) {
+            ok = false;
+            break;
+          }
+          if (globaltimer_ns() - t0 > p.timeout_ns) {
+            set_error(p, PKT_DEV_TIMEOUT_DEPS, t, r1 != 0 ? r1 : r2);
+            ok = false;
+            break;
+          }
+        }
+        __nanosleep(32);
+      }
+      dep_cycles += clock64() - c0;
+      if (!ok) break;
+    }
+    // ---- publish into the slot ring
+    const int slot = seq % kSlots;
+    const long long c1 = clock64();
+    if (!wait_bar(p, &s.slot_empty[slot], ((seq / kSlots) & 1) ^ 1, 1)) break;
+    slot_cycles += clock64() - c1;
+    task.header.user_tag = uint32_t(t);
+    copy_task(&s.slots[slot], &task);
+    if (p.task_counter) atomicAdd(p.task_counter, 1ull);
+    mbar_arrive(&s.slot_full[slot]);
+    ++seq;
+    ++ntasks;
+  }
+  // ---- stop marker: consumers leave their loops when they reach it
+  const int slot = seq % kSlots;
+  if (wait_bar(p, &s.slot_empty[slot], ((seq / kSlots) & 1) ^ 1, 2)) {
+    s.slots[slot].header.opcode = kOpStop;
+    mbar_arrive(&s.slot_full[slot]);
+  }
+  if (perf) {
+    perf[kPerfTasks] = ntasks;
+    perf[kPerfCtrlDepWait] = dep_cycles;
+    perf[kPerfCtrlSlotWait] = slot_cycles;
+  }
+}
+
+// ============================================================ loader (TMA producer)
+__device__ void loader_loop(const KParams& p, Smem& s, unsigned long long* perf) {
+  int seq = 0;
+  uint32_t stage = 0, phase = 0, issued = 0;
+  unsigned long long wait_cycles = 0;
+  while (true) {
+    const int slot = seq % kSlots;
+    if (!wait_bar(p, &s.slot_full[slot], (seq / kSlots) & 1, 3, true)) break;
+    const uint16_t op = s.slots[slot].header.opcode;
+    pkt_gemm_tile_args ga = *reinterpret_cast<const pkt_gemm_tile_args*>(s.slots[slot].args);
+    mbar_arrive(&s.slot_empty[slot]);
+    ++seq;
+    if (op == kOpStop) break;
+    if (op != PKT_OP_GEMM) continue;
+    const DevGemm& g = p.gemms[ga.gemm];
+    // Data of this tile was produced by other CTAs through generic stores and is
+    // read here through the async proxy.
+    fence_proxy_async_global();
+    const int m0 = int(ga.tile_m) * kBM;
+    const int n0 = int(ga.tile_n) * g.d.bn;
+    bool ok = true;
+    for (int kb = 0; kb < g.num_kb; ++kb) {
+      const long long c0 = clock64();
+      if (!wait_bar(p, &s.empty[stage], phase ^ 1, 4)) {
+        ok = false;
+        break;
+      }
+      wait_cycles += clock64() - c0;
+      mbar_arrive_expect_tx(&s.full[stage], g.stage_tx);
+      uint8_t* sa = s.stages[stage];
+      uint8_t* sb = s.stages[stage] + kATileBytes;
+      const int k0 = kb * g.bk;
+      if (g.d.a_major == PKT_MAJOR_K) {
+        tma_load_2d(sa, &g.map_a, &s.full[stage], k0, m0);
+      } else {
+        for (int i = 0; i < g.a_boxes; ++i)
+          tma_load_2d(sa + i * g.a_box_bytes, &g.map_a, &s.full[stage], m0 + i * g.box_mn, k0);
+      }
+      if (g.d.b_major == PKT_MAJOR_K) {
+        tma_load_2d(sb, &g.map_b, &s.full[stage], k0, n0);
+      } else {
+        for (int i = 0; i < g.b_boxes; ++i)
+          tma_load_2d(sb + i * g.b_box_bytes, &g.map_b, &s.full[stage], n0 + i * g.box_mn, k0);
+      }
+      ++issued;
+      if (++stage == kStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    if (!ok) break;
+  }
+  // Drain: wait (bounded) until every issued stage landed, so no bulk copy can
+  // write into this CTA's shared memory after it exits.
+  const uint32_t n = issued < kStages ? issued : kStages;
+  for (uint32_t i = 0; i < n; ++i) {
+    const uint32_t idx = (stage + kStages - 1 - i) % kStages;
+    const uint32_t fill = issued - 1 - i;  // fill number of that stage
+    const uint32_t par = (fill / kStages) & 1;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&s.full[idx], par)) {
+      if (globaltimer_ns() - t0 > p.timeout_ns) break;
+    }
+  }
+  if (perf) perf[kPerfLoadStageWait] = wait_cycles;
+}
+
+// ============================================================ MMA issuer
+__device__ void mma_loop(const KParams& p, Smem& s, uint32_t tmem_base,
+                         unsigned long long* perf) {
+  int seq = 0;
+  uint32_t stage = 0, phase = 0, gemm_count = 0;
+  unsigned long long full_wait = 0, tmem_wait = 0, tiles = 0;
+  bool any_mma = false;
+  while (true) {
+    const int slot = seq % kSlots;
+    if (!wait_bar(p, &s.slot_full[slot], (seq / kSlots) & 1, 5, true)) break;
+    const uint16_t op = s.slots[slot].header.opcode;
+    pkt_gemm_tile_args ga = *reinterpret_cast<const pkt_gemm_tile_args*>(s.slots[slot].args);
+    mbar_arrive(&s.slot_empty[slot]);
+    ++seq;
+    if (op == kOpStop) break;
+    if (op != PKT_OP_GEMM) continue;
+    const DevGemm& g = p.gemms[ga.gemm];
+    const uint32_t acc = gemm_count & 1, use = gemm_count >> 1;
+    const long long c0 = clock64();
+    if (!wait_bar(p, &s.tmem_empty[acc], (use & 1) ^ 1, 6)) break;
+    tmem_wait += clock64() - c0;
+    tc_fence_after();
+    const uint32_t d_tmem = tmem_base + acc * 256;
+    const bool tf32 = g.d.in_dtype == PKT_DTYPE_TF32;
+    bool ok = true;
+    for (int kb = 0; kb < g.num_kb; ++kb) {
+      const long long c1 = clock64();
+      if (!wait_bar(p, &s.full[stage], phase, 7)) {
+        ok = false;
+        break;
+      }
+      full_wait += clock64() - c1;
+      tc_fence_after();
+      const uint32_t sa = smem_u32(s.stages[stage]);
+      const uint32_t sb = sa + kATileBytes;
+#pragma unroll 1
+      for (int k = 0; k < g.mma_per_kb; ++k) {
+        const uint64_t ad = smem_desc(sa + k * g.a_kstep, g.a_lbo, g.a_sbo, g.a_layout);
+        const uint64_t bd = smem_desc(sb + k * g.b_kstep, g.b_lbo, g.b_sbo, g.b_layout);
+        const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+        if (tf32)
+          mma_tf32(d_tmem, ad, bd, g.idesc, accum);
+        else
+          mma_bf16(d_tmem, ad, bd, g.idesc, accum);
+      }
+      any_mma = true;
+      mma_commit(&s.empty[stage]);  // stage reusable once these MMAs have read it
+      if (++stage == kStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    if (!ok) break;
+    mma_commit(&s.tmem_full[acc]);  // accumulator complete
+    ++gemm_count;
+    ++tiles;
+  }
+  if (any_mma) {
+    // Every MMA this thread issued has finished before TMEM is released.
+    mma_commit(&s.mma_drain);
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&s.mma_drain, 0)) {
+      if (globaltimer_ns() - t0 > p.timeout_ns) break;
+    }
+  }
+  if (perf) {
+    perf[kPerfGemmTiles] = tiles;
+    perf[kPerfMmaFullWait] = full_wait;
+    perf[kPerfMmaTmemWait] = tmem_wait;
+  }
+}
+
+// ============================================================ epilogue helpers
+struct EpiCtx {
+  int et;    // 0..127 thread index among the compute warps
+  int lane;
+  int q;     // TMEM lane quadrant of this warp (warp id % 4)
+};
+
+__device__ __forceinline__ void epi_sync() { named_barrier_sync(1, kEpiThreads); }
+
+// Transpose-reduce: on entry each lane holds 32 column values of its row; on
+// exit lane l holds the sum over the warp's 32 rows of column l.
+__device__ __forceinline__ float warp_column_sums(float (&v)[32], int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int j = 0; j < off; ++j) {
+      const float send = upper ? v[j] : v[j + off];
+      const float keep = upper ? v[j + off] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
+}
+
+__device__ __forceinline__ float load_elem(const void* base, int dtype, long long idx) {
+  if (dtype == PKT_DTYPE_BF16) {
+    const uint16_t h = reinterpret_cast<const uint16_t*>(base)[idx];
+    return __uint_as_float(uint32_t(h) << 16);
+  }
+  return reinterpret_cast<const float*>(base)[idx];
+}
+
+// Loads 32 consecutive elements (bf16 or fp32 storage) of one row into v.
+__device__ __forceinline__ void load_row32(const void* base, int dtype, long long idx, int nvalid,
+                                           bool vec, float (&v)[32]) {
+  if (vec && nvalid == 32) {
+    if (dtype == PKT_DTYPE_BF16) {
+      const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + idx);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 w = p[i];
+        v[8 * i + 0] = bf16_lo(w.x);
+        v[8 * i + 1] = bf16_hi(w.x);
+        v[8 * i + 2] = bf16_lo(w.y);
+        v[8 * i + 3] = bf16_hi(w.y);
+        v[8 * i + 4] = bf16_lo(w.z);
+        v[8 * i + 5] = bf16_hi(w.z);
+        v[8 * i + 6] = bf16_lo(w.w);
+        v[8 * i + 7] = bf16_hi(w.w);
+      }
+    } else {
+      const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 w = p[i];
+        v[4 * i + 0] = w.x;
+        v[4 * i + 1] = w.y;
+        v[4 * i + 2] = w.z;
+        v[4 * i + 3] = w.w;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (j < nvalid) ? load_elem(base, dtype, idx + j) : 0.f;
+  }
+}
+
+// Rounds v to the storage type in place (so later reductions see stored values)
+// and stores the valid part.
+__device__ __forceinline__ void store_row32(void* base, int dtype, long long idx, int nvalid,
+                                            bool vec, float (&v)[32]) {
+  if (dtype == PKT_DTYPE_BF16) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      v[2 * i] = bf16_lo(pk[i]);
+      v[2 * i + 1] = bf16_hi(pk[i]);
+    }
+    uint16_t* b = reinterpret_cast<uint16_t*>(base) + idx;
+    if (vec && nvalid == 32) {
+      uint4* p = reinterpret_cast<uint4*>(b);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        p[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nvalid) b[j] = uint16_t((j & 1) ? (pk[j >> 1] >> 16) : (pk[j >> 1] & 0xffffu));
+    }
+  } else {
+    float* f = reinterpret_cast<float*>(base) + idx;
+    if (vec && nvalid == 32) {
+      float4* p = reinterpret_cast<float4*>(f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nvalid) f[j] = v[j];
+    }
+  }
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// ============================================================ GEMM epilogue
+__device__ void epilogue_gemm(const KParams& p, Smem& s, const EpiCtx& c, const DevGemm& g,
+                              int tile_m, int tile_n, uint32_t tmem_base, uint32_t acc,
+                              uint32_t use, unsigned long long& tmem_wait) {
+  const pkt_gemm_desc& d = g.d;
+  const long long c0 = clock64();
+  wait_bar(p, &s.tmem_full[acc], use & 1, 8);
+  tmem_wait += clock64() - c0;
+  __syncwarp();  // tcgen05.ld is warp-collective
+  tc_fence_after();
+
+  const int row = tile_m * kBM + c.q * 32 + c.lane;
+  const bool row_ok = row < d.M;
+  const int n0 = tile_n * d.bn;
+  const int nchunks = (d.bn + 31) / 32;
+  const int epi = d.epilogue;
+  const bool want_colsum = (epi == PKT_EPI_MSE || epi == PKT_EPI_DGRAD_RELU) && d.colsum != nullptr;
+  const int out_es = d.out_dtype == PKT_DTYPE_BF16 ? 2 : 4;
+  const int in_es = d.in_dtype == PKT_DTYPE_BF16 ? 2 : 4;
+  float loss = 0.f;
+
+  for (int ch = 0; ch < nchunks; ++ch) {
+    uint32_t r[32];
+    const uint32_t taddr = tmem_base + (uint32_t(c.q * 32) << 16) + acc * 256 + ch * 32;
+    tmem_ld32(taddr, r);
+    tmem_ld_wait();
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    const int col0 = n0 + ch * 32;
+    int nvalid = min(d.N - col0, d.bn - ch * 32);  // inside the matrix and inside this tile
+    nvalid = nvalid < 0 ? 0 : (nvalid > 32 ? 32 : nvalid);
+    if (!row_ok) nvalid = 0;
+
+    if (epi == PKT_EPI_STORE || epi == PKT_EPI_WGRAD_STORE) {
+      const long long o = (long long)row * d.ldo + col0;
+      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(d.out) + o * out_es);
+      if (nvalid > 0) store_row32(d.out, d.out_dtype, o, nvalid, vec, v);
+    } else if (epi == PKT_EPI_BIAS_ACT) {
+      if (d.bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += (col0 + j < d.N) ? __ldg(d.bias + col0 + j) : 0.f;
+      }
+      if (d.relu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+      }
+      const long long o = (long long)row * d.ldo + col0;
+      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(d.out) + o * out_es);
+      if (nvalid > 0) store_row32(d.out, d.out_dtype, o, nvalid, vec, v);
+    } else if (epi == PKT_EPI_MSE) {
+      if (d.bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += (col0 + j < d.N) ? __ldg(d.bias + col0 + j) : 0.f;
+      }
+      if (d.relu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+      }
+      if (d.y_out != nullptr && nvalid > 0) {
+        float y[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = v[j];
+        const long long oy = (long long)row * d.ldy + col0;
+        store_row32(d.y_out, PKT_DTYPE_F32, oy, nvalid,
+                    aligned16(reinterpret_cast<const float*>(d.y_out) + oy), y);
+      }
+      float t[32];
+      const long long oa = (long long)row * d.ldaux + col0;
+      const bool avec = aligned16(reinterpret_cast<const uint8_t*>(d.aux) + oa * in_es);
+      if (nvalid > 0) {
+        load_row32(d.aux, d.in_dtype, oa, nvalid, avec, t);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) t[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float diff = v[j] - t[j];
+        const bool ok = j < nvalid;
+        loss += ok ? diff * diff : 0.f;
+        float gr = d.scale * diff;
+        if (d.relu && v[j] <= 0.f) gr = 0.f;
+        v[j] = ok ? gr : 0.f;
+      }
+      const long long o = (long long)row * d.ldo + col0;
+      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(d.out) + o * out_es);
+      if (nvalid > 0) store_row32(d.out, d.out_dtype, o, nvalid, vec, v);
+    } else if (epi == PKT_EPI_DGRAD_RELU) {
+      float h[32];
+      const long long oa = (long long)row * d.ldaux + col0;
+      const bool avec = aligned16(reinterpret_cast<const uint8_t*>(d.aux) + oa * in_es);
+      if (nvalid > 0) {
+        load_row32(d.aux, d.in_dtype, oa, nvalid, avec, h);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) h[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = (j < nvalid && h[j] > 0.f) ? v[j] : 0.f;
+      const long long o = (long long)row * d.ldo + col0;
+      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(d.out) + o * out_es);
+      if (nvalid > 0) store_row32(d.out, d.out_dtype, o, nvalid, vec, v);
+    } else if (epi == PKT_EPI_WGRAD_SGD) {
+      float w[32];
+      const long long ow = (long long)row * d.ldw + col0;
+      const bool wvec = aligned16(d.w_in + ow) && aligned16(d.w_out + ow);
+      if (nvalid > 0) {
+        load_row32(d.w_in, PKT_DTYPE_F32, ow, nvalid, wvec, w);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = fmaf(-d.lr, v[j], w[j]);
+        float w2[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w2[j] = w[j];
+        store_row32(d.w_out, PKT_DTYPE_F32, ow, nvalid, wvec, w);
+        if (d.w_shadow) {
+          const bool svec = aligned16(reinterpret_cast<const uint16_t*>(d.w_shadow) + ow);
+          store_row32(d.w_shadow, PKT_DTYPE_BF16, ow, nvalid, svec, w2);
+        }
+      }
+    }
+
+    if (want_colsum) {
+      // v holds the stored (rounded) values, zero outside the valid region.
+      const float cs = warp_column_sums(v, c.lane);
+      s.red[ch][c.q][c.lane] = cs;
+    }
+  }
+  // Accumulator fully read: hand it back to the MMA warp.
+  tc_fence_before();
+  __syncwarp();
+  if (c.lane == 0) mbar_arrive(&s.tmem_empty[acc]);
+
+  if (epi == PKT_EPI_MSE && d.loss_partials != nullptr) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) loss += __shfl_xor_sync(0xffffffffu, loss, off);
+    if (c.lane == 0) s.lossred[c.q] = loss;
+  }
+  if (want_colsum || (epi == PKT_EPI_MSE && d.loss_partials != nullptr)) {
+    epi_sync();
+    if (want_colsum) {
+      for (int i = c.et; i < nchunks * 32; i += kEpiThreads) {
+        const int ch = i >> 5, j = i & 31;
+        const int col = n0 + ch * 32 + j;
+        if (col < d.N && ch * 32 + j < d.bn) {
+          const float tot = ((s.red[ch][0][j] + s.red[ch][1][j]) + s.red[ch][2][j]) + s.red[ch][3][j];
+          d.colsum[(long long)tile_m * d.ldcol + col] = tot;
+        }
+      }
+    }
+    if (epi == PKT_EPI_MSE && d.loss_partials != nullptr && c.et == 0) {
+      d.loss_partials[tile_m * g.tiles_n + tile_n] =
+          ((s.lossred[0] + s.lossred[1]) + s.lossred[2]) + s.lossred[3];
+    }
+  }
+}
+
+// ============================================================ SIMT ops (128 threads)
+__device__ void op_axpy(const AxpyArgs& a, int et) {
+  const long long n = a.n;
+  if (aligned16(a.x) && aligned16(a.y)) {
+    const long long n4 = n >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    float4* y4 = reinterpret_cast<float4*>(a.y);
+    long long i = et;
+    for (; i + 3 * kEpiThreads < n4; i += 4 * kEpiThreads) {
+      float4 xv[4], yv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        xv[u] = x4[i + u * kEpiThreads];
+        yv[u] = y4[i + u * kEpiThreads];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        yv[u].x = fmaf(a.a, xv[u].x, yv[u].x);
+        yv[u].y = fmaf(a.a, xv[u].y, yv[u].y);
+        yv[u].z = fmaf(a.a, xv[u].z, yv[u].z);
+        yv[u].w = fmaf(a.a, xv[u].w, yv[u].w);
+        y4[i + u * kEpiThreads] = yv[u];
+      }
+    }
+    for (; i < n4; i += kEpiThreads) {
+      const float4 xv = x4[i];
+      float4 yv = y4[i];
+      yv.x = fmaf(a.a, xv.x, yv.x);
+      yv.y = fmaf(a.a, xv.y, yv.y);
+      yv.z = fmaf(a.a, xv.z, yv.z);
+      yv.w = fmaf(a.a, xv.w, yv.w);
+      y4[i] = yv;
+    }
+    for (long long k = n4 * 4 + et; k < n; k += kEpiThreads) a.y[k] = fmaf(a.a, a.x[k], a.y[k]);
+  } else {
+    for (long long k = et; k < n; k += kEpiThreads) a.y[k] = fmaf(a.a, a.x[k], a.y[k]);
+  }
+}
+
+__device__ void op_zero(const ZeroMemoryArgs& a, int et) {
+  const long long n = a.size;
+  if (aligned16(a.ptr)) {
+    const long long n4 = n >> 2;
+    float4* p4 = reinterpret_cast<float4*>(a.ptr);
+    for (long long i = et; i < n4; i += kEpiThreads) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (long long k = n4 * 4 + et; k < n; k += kEpiThreads) a.ptr[k] = 0.f;
+  } else {
+    for (long long k = et; k < n; k += kEpiThreads) a.ptr[k] = 0.f;
+  }
+}
+
+// w_out = w - lr*g (single-rounding fma, as nvcc compiles pkt's `W[i] -= lr*dW[i]`,
+// include/ops/sgd.cuh:41-43), optionally also writing the bf16 copy of w_out.
+__device__ void op_sgd(const float* W, const float* dW, float* Wo, float lr, long long n,
+                       uint16_t* shadow, int et) {
+  const bool vec = aligned16(W) && aligned16(dW) && aligned16(Wo) &&
+                   (shadow == nullptr || (reinterpret_cast<uintptr_t>(shadow) & 7u) == 0);
+  long long head = 0;
+  if (vec) {
+    const long long n4 = n >> 2;
+    const float4* w4 = reinterpret_cast<const float4*>(W);
+    const float4* g4 = reinterpret_cast<const float4*>(dW);
+    float4* o4 = reinterpret_cast<float4*>(Wo);
+    long long i = et;
+    for (; i + 3 * kEpiThreads < n4; i += 4 * kEpiThreads) {
+      float4 w[4], g[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        w[u] = w4[i + u * kEpiThreads];
+        g[u] = g4[i + u * kEpiThreads];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        w[u].x = fmaf(-lr, g[u].x, w[u].x);
+        w[u].y = fmaf(-lr, g[u].y, w[u].y);
+        w[u].z = fmaf(-lr, g[u].z, w[u].z);
+        w[u].w = fmaf(-lr, g[u].w, w[u].w);
+        o4[i + u * kEpiThreads] = w[u];
+        if (shadow)
+          reinterpret_cast<uint2*>(shadow)[i + u * kEpiThreads] =
+              make_uint2(pack_bf16x2(w[u].x, w[u].y), pack_bf16x2(w[u].z, w[u].w));
+      }
+    }
+    for (; i < n4; i += kEpiThreads) {
+      float4 w = w4[i];
+      const float4 g = g4[i];
+      w.x = fmaf(-lr, g.x, w.x);
+      w.y = fmaf(-lr, g.y, w.y);
+      w.z = fmaf(-lr, g.z, w.z);
+      w.w = fmaf(-lr, g.w, w.w);
+      o4[i] = w;
+      if (shadow)
+        reinterpret_cast<uint2*>(shadow)[i] = make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
+    }
+    head = n4 * 4;
+  }
+  for (long long k = head + et; k < n; k += kEpiThreads) {
+    const float w = fmaf(-lr, dW[k], W[k]);
+    Wo[k] = w;
+    if (shadow) shadow[k] = f32_to_bf16_rn(w);
+  }
+}
+
+// Deterministic sum over the 128 compute threads (fixed order), result on et == 0.
+__device__ float epi_block_sum(Smem& s, const EpiCtx& c, float v) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  if (c.lane == 0) s.simt_red[c.et >> 5] = v;
+  epi_sync();
+  float tot = ((s.simt_red[0] + s.simt_red[1]) + s.simt_red[2]) + s.simt_red[3];
+  epi_sync();
+  return tot;
+}
+
+__device__ void op_mse(Smem& s, const EpiCtx& c, const MSELossArgs& a) {
+  const long long elems = (long long)a.batch * a.m;
+  const float scale = 2.0f / float(a.batch * a.m);
+  float part = 0.f;
+  for (long long i = c.et; i < elems; i += kEpiThreads) {
+    const float diff = a.y[i] - a.target[i];
+    a.dy[i] = scale * diff;
+    part = fmaf(diff, diff, part);
+  }
+  const float tot = epi_block_sum(s, c, part);
+  if (c.et == 0) atomicAdd(a.loss, tot / float(elems));
+}
+
+__device__ void op_linear_forward(const LinearForwardArgs& a, int et) {
+  // y[b, j] = sum_k x[b, k] W[j, k] over the task's tile (include/ops/linear_fwd.cuh:18-29),
+  // fp32 throughout (pkt rounds x to fp16 first; this path keeps full fp32).
+  const int rows = a.tile_m_count, cols = a.tile_n_count;
+  const long long total = (long long)rows * cols;
+  for (long long o = et; o < total; o += kEpiThreads) {
+    const int b = a.tile_m_start + int(o / cols);
+    const int j = a.tile_n_start + int(o % cols);
+    if (b >= a.batch || j >= a.m) continue;
+    const float* xr = a.x + (long long)b * a.n;
+    const float* wr = a.W + (long long)j * a.n;
+    float acc = 0.f;
+    for (int k = 0; k < a.n; ++k) acc = fmaf(xr[k], wr[k], acc);
+    a.y[(long long)b * a.m + j] = acc;
+  }
+}
+
+__device__ void op_linear_backward(const LinearBackwardArgs& a, int et) {
+  // dW[r, c] = sum_b dy[b, r] x[b, c], overwriting the tile (include/ops/linear_bwd.cuh:94-157).
+  const int rows = a.tile_m_count, cols = a.tile_n_count;
+  const long long total = (long long)rows * cols;
+  for (long long o = et; o < total; o += kEpiThreads) {
+    const int r = a.tile_m_start + int(o / cols);
+    const int cc = a.tile_n_start + int(o % cols);
+    if (r >= a.m || cc >= a.n) continue;
+    float acc = 0.f;
+    for (int b = 0; b < a.batch; ++b) acc = fmaf(a.dy[(long long)b * a.m + r], a.x[(long long)b * a.n + cc], acc);
+    a.dW[(long long)r * a.n + cc] = acc;
+  }
+}
+
+__device__ void op_bias_sgd(const pkt_bias_sgd_args& a, int et) {
+  for (int col = a.col_begin + et; col < a.col_end; col += kEpiThreads) {
+    float sum = 0.f;
+    for (int pidx = 0; pidx < a.num_partials; ++pidx) sum += a.partials[(long long)pidx * a.ld + col];
+    if (a.grad_out) a.grad_out[col] = sum;
+    if (a.bias) a.bias[col] = fmaf(-a.lr, sum, a.bias[col]);
+  }
+}
+
+__device__ void op_loss_reduce(Smem& s, const EpiCtx& c, const pkt_loss_reduce_args& a) {
+  double part = 0.0;
+  for (int i = c.et; i < a.count; i += kEpiThreads) part += double(a.partials[i]);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+  if (c.lane == 0) s.simt_redd[c.et >> 5] = part;
+  epi_sync();
+  if (c.et == 0) {
+    const double tot = ((s.simt_redd[0] + s.simt_redd[1]) + s.simt_redd[2]) + s.simt_redd[3];
+    float* dst = a.loss;
+    if (a.step) dst += (*a.step)++;
+    *dst = float(tot * double(a.scale));
+  }
+  epi_sync();
+}
+
+// ============================================================ compute warps
+__device__ void compute_loop(const KParams& p, Smem& s, uint32_t tmem_base, const EpiCtx& c,
+                             unsigned long long* perf) {
+  int seq = 0;
+  uint32_t gemm_count = 0;
+  unsigned long long tmem_wait = 0, gemm_cycles = 0, simt_cycles = 0;
+  while (true) {
+    const int slot = seq % kSlots;
+    if (!wait_bar(p, &s.slot_full[slot], (seq / kSlots) & 1, 9, true)) break;
+    pkt_task task;
+    copy_task(&task, &s.slots[slot]);
+    epi_sync();  // every compute thread has its copy
+    if (c.et == 0) mbar_arrive(&s.slot_empty[slot]);
+    ++seq;
+    const uint16_t op = task.header.opcode;
+    if (op == kOpStop) break;
+    const long long c0 = clock64();
+    switch (op) {
+      case PKT_OP_GEMM: {
+        const pkt_gemm_tile_args& ga = *reinterpret_cast<const pkt_gemm_tile_args*>(task.args);
+        const uint32_t acc = gemm_count & 1, use = gemm_count >> 1;
+        epilogue_gemm(p, s, c, p.gemms[ga.gemm], int(ga.tile_m), int(ga.tile_n), tmem_base, acc,
+                      use, tmem_wait);
+        ++gemm_count;
+        break;
+      }
+      case PKT_OP_AXPY:
+        op_axpy(*reinterpret_cast<const AxpyArgs*>(task.args), c.et);
+        break;
+      case PKT_OP_ZERO_MEMORY:
+        op_zero(*reinterpret_cast<const ZeroMemoryArgs*>(task.args), c.et);
+        break;
+      case PKT_OP_SGD_UPDATE: {
+        const SGDUpdateArgs& a = *reinterpret_cast<const SGDUpdateArgs*>(task.args);
+        op_sgd(a.W, a.dW, a.W, a.lr, a.size, nullptr, c.et);
+        break;
+      }
+      case PKT_OP_SGD_MIXED: {
+        const pkt_sgd_mixed_args& a = *reinterpret_cast<const pkt_sgd_mixed_args*>(task.args);
+        op_sgd(a.w, a.g, a.w_out ? a.w_out : const_cast<float*>(a.w), a.lr, a.n, a.w_bf16, c.et);
+        break;
+      }
+      case PKT_OP_MSE_LOSS:
+        op_mse(s, c, *reinterpret_cast<const MSELossArgs*>(task.args));
+        break;
+      case PKT_OP_LINEAR_FORWARD:
+        op_linear_forward(*reinterpret_cast<const LinearForwardArgs*>(task.args), c.et);
+        break;
+      case PKT_OP_LINEAR_BACKWARD:
+        op_linear_backward(*reinterpret_cast<const LinearBackwardArgs*>(task.args), c.et);
+        break;
+      case PKT_OP_BIAS_SGD:
+        op_bias_sgd(*reinterpret_cast<const pkt_bias_sgd_args*>(task.args), c.et);
+        break;
+      case PKT_OP_LOSS_REDUCE:
+        op_loss_reduce(s, c, *reinterpret_cast<const pkt_loss_reduce_args*>(task.args));
+        break;
+      default:  // PKT_OP_INVALID: no work, tokens are still published
+        break;
+    }
+    if (op == PKT_OP_GEMM)
+      gemm_cycles += clock64() - c0;
+    else
+      simt_cycles += clock64() - c0;
+    // ---- publish completion: stores visible at gpu scope (and to the async
+    // proxy of consumers' TMA loads) before the release on the token.
+    __threadfence();
+    fence_proxy_async_global();
+    epi_sync();
+    if (c.et == 0) {
+      const pkt_task_header& h = task.header;
+      if (h.buffer_write_id != 0) {
+        atomicMax(tok_epoch(p) + h.buffer_write_id, int(h.write_epoch));
+        red_release_gpu_add(tok_count(p) + h.buffer_write_id, 1);
+      }
+      const int w2 = int(h.ext_ids >> 16);
+      if (w2 != 0) red_release_gpu_add(tok_count(p) + w2, 1);
+    }
+  }
+  if (perf && c.et == 0) {
+    perf[kPerfEpiTmemWait] = tmem_wait;
+    perf[kPerfEpiGemm] = gemm_cycles;
+    perf[kPerfEpiSimt] = simt_cycles;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) pk_megakernel(const __grid_constant__ KParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                     ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  unsigned long long* perf = p.perf ? p.perf + (size_t)blockIdx.x * PKT_PERF_WORDS : nullptr;
+  const long long t_start = clock64();
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&s.slot_full[i], 1);
+      mbar_init(&s.slot_empty[i], 3);  // loader, MMA issuer, compute warps
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tmem_full[i], 1);
+      mbar_init(&s.tmem_empty[i], 4);  // one arrive per compute warp
+    }
+    mbar_init(&s.mma_drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&s.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+
+  if (warp == kCtrlWarp) {
+    if (lane == 0) controller_loop(p, s, perf);
+    __syncwarp();
+  } else if (warp == kLoadWarp) {
+    if (lane == 0) loader_loop(p, s, perf);
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) mma_loop(p, s, tmem_base, perf);
+    __syncwarp();
+  } else {
+    EpiCtx c{int(threadIdx.x) - kEpiWarp0 * 32, lane, warp & 3};
+    compute_loop(p, s, tmem_base, c, perf);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (perf && threadIdx.x == 0) perf[kPerfTotal] = clock64() - t_start;
+}
+
+}  // namespace
+
+int megakernel_smem_bytes() { return kSmemBytes; }
+
+cudaError_t launch_megakernel(const KParams& p, int blocks, cudaStream_t stream) {
+  // The attribute is per device; set it on every device this process launches on.
+  static unsigned long long attr_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !(attr_mask & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(pk_megakernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_mask |= 1ull << dev;
+  }
+  pk_megakernel<<<blocks, kThreads, kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace pkb

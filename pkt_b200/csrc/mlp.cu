@@ -1,0 +1,766 @@
+// MLP training engine: the multi-layer generalisation of pkt's train_linear
+// (examples/train_linear.cu:482-607 builds one Linear's forward / MSE /
+// backward / SGD task DAG). Here one training step is ONE persistent launch of
+// a tile-granular DAG:
+//
+//   FWD(l, i, j)   tcgen05 tile of H_{l+1} = act(H_l W_l^T + b_l), row block i
+//                  waits on F[l-1][i] (all column tiles of row block i of the
+//                  previous layer); the last layer's epilogue is MSE: it writes
+//                  dY = 2(y-t)/(B n), per-tile loss partials and column sums of dY
+//   LOSS_REDUCE    deterministic sum of the loss partials -> losses[step]
+//   DGRAD(l, i, j) tile of dY_{l-1} = (dY_l W_l) * [H_l > 0], waits on row block i of dY_l
+//   WGRAD(l, p, q) tile of dW_l = dY_l^T H_l (K = batch) with SGD fused into the
+//                  epilogue (fp32 master update + bf16 copy for the next step),
+//                  waits on all of dY_l
+//   BIAS_SGD(l)    b_l -= lr * (sum of dY_l column partials)
+//
+// Weights the GEMMs read are double-buffered by step parity (bf16 copies, or
+// the fp32 masters in TF32 mode), so the fused SGD of step s never races the
+// forward / dgrad reads of step s.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "internal.h"
+#include "runtime_impl.h"
+
+namespace pkb {
+
+namespace {
+
+__global__ void f32_to_bf16_2d(const float* src, int rows, int cols, int lds, uint16_t* dst,
+                               int ldd) {
+  const long long total = (long long)rows * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int r = int(i / cols), c = int(i % cols);
+    const float f = src[(long long)r * lds + c];
+    uint16_t h;
+    asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(f));
+    dst[(long long)r * ldd + c] = h;
+  }
+}
+
+inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+}  // namespace
+
+struct Mlp {
+  Runtime* rt = nullptr;
+  int L = 0, B = 0;
+  std::vector<int> dims, ld;
+  bool bf = true;  // bf16 mode (else tf32)
+  int es = 2;      // storage bytes per activation element
+  bool has_bias = true, relu_last = false;
+  float lr = 1e-3f;
+  int grad_mode = 0;
+  int max_bn = 256;
+  float grad_scale = 1.0f;
+  bool capture_y = false;
+
+  void* X = nullptr;
+  void* T = nullptr;
+  std::vector<void*> H;   // H[l], l = 1..L-1 (index 0 unused)
+  std::vector<void*> dY;  // dY[l], l = 0..L-1
+  std::vector<float*> W32[2];
+  std::vector<uint16_t*> Wbf[2];
+  std::vector<float*> bias;
+  std::vector<float*> colsum;
+  float* loss_partials = nullptr;
+  float* losses = nullptr;
+  int* step_ctr = nullptr;
+  int loss_cap = 1 << 16;
+  int losses_enqueued = 0;
+  float* Yout = nullptr;
+  float* grads = nullptr;  // grad_mode 1: flat [dW_0 .. dW_{L-1}, db_0 .. db_{L-1}]
+  long long grad_count = 0;
+  std::vector<long long> dW_off, db_off;
+
+  int parity = 0;
+  int TM = 0;
+  std::vector<pkt_task> tasks[2], update[2];
+  pkt_task* d_tasks[2] = {nullptr, nullptr};
+  pkt_task* d_update[2] = {nullptr, nullptr};
+  int num_tokens = 0;
+  int gemm_tiles_per_step = 0;
+  double flops_per_step = 0;
+
+  ~Mlp() {
+    if (rt) cudaSetDevice(rt->device);
+    auto F = [](void* p) { cudaFree(p); };
+    F(X);
+    F(T);
+    for (auto p : H) F(p);
+    for (auto p : dY) F(p);
+    for (int k = 0; k < 2; ++k) {
+      for (auto p : W32[k]) F(p);
+      for (auto p : Wbf[k]) F(p);
+      F(d_tasks[k]);
+      F(d_update[k]);
+    }
+    for (auto p : bias) F(p);
+    for (auto p : colsum) F(p);
+    F(loss_partials);
+    F(losses);
+    F(step_ctr);
+    F(Yout);
+    F(grads);
+    delete rt;
+  }
+
+  int act_dtype() const { return bf ? PKT_DTYPE_BF16 : PKT_DTYPE_F32; }
+  int in_dtype() const { return bf ? PKT_DTYPE_BF16 : PKT_DTYPE_TF32; }
+  const void* Hin(int l) const { return l == 0 ? X : H[l]; }
+  // weight copy the GEMMs of parity p read
+  const void* Wop(int l, int p) const { return bf ? (const void*)Wbf[p][l] : (const void*)W32[p][l]; }
+  float* Wmaster(int l, int p) const { return bf ? W32[0][l] : W32[p][l]; }
+
+  int pick_bn(int M, int N, bool b_mn) const {
+    const int align = b_mn ? (bf ? 64 : 32) : 16;
+    int cap = std::min(max_bn, kMaxBN);
+    int need = round_up(N, align);
+    int bn = std::min(cap, need);
+    bn = std::max(align, bn / align * align);
+    const int tiles_m = (M + kBM - 1) / kBM;
+    // shrink the tile until the GEMM alone fills the SMs (small layers)
+    while (bn > std::max(64, align) && (long long)tiles_m * ((N + bn - 1) / bn) < rt->num_sms) {
+      const int nb = bn / 2;
+      if (nb % align != 0) break;
+      bn = nb;
+    }
+    return bn;
+  }
+
+  int alloc(void** p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, std::max<size_t>(bytes, 16));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(mlp buffer)");
+    cudaMemset(*p, 0, std::max<size_t>(bytes, 16));
+    return PKT_OK;
+  }
+
+  int setup(const pkt_mlp_config& c);
+  int build(int p);
+  int launch_list(pkt_task* d, int n, cudaStream_t st);
+};
+
+int Mlp::setup(const pkt_mlp_config& c) {
+  L = c.num_layers;
+  B = c.batch;
+  if (L <= 0 || B <= 0 || !c.dims) return fail(PKT_ERR_ARGS, "bad MLP config");
+  dims.assign(c.dims, c.dims + L + 1);
+  for (int d : dims)
+    if (d <= 0) return fail(PKT_ERR_ARGS, "layer widths must be positive");
+  if (c.dtype != PKT_DTYPE_BF16 && c.dtype != PKT_DTYPE_TF32) return fail(PKT_ERR_ARGS, "dtype must be bf16 or tf32");
+  bf = c.dtype == PKT_DTYPE_BF16;
+  es = bf ? 2 : 4;
+  has_bias = c.has_bias != 0;
+  relu_last = c.relu_last != 0;
+  lr = c.lr;
+  grad_mode = c.grad_mode;
+  max_bn = c.max_bn > 0 ? c.max_bn : 256;
+  if (grad_mode != 0 && grad_mode != 1) return fail(PKT_ERR_ARGS, "grad_mode must be 0 or 1");
+  ld.resize(L + 1);
+  for (int l = 0; l <= L; ++l) ld[l] = round_up(dims[l], 64);
+  TM = (B + kBM - 1) / kBM;
+  int rc;
+  if ((rc = alloc(&X, size_t(B) * ld[0] * es))) return rc;
+  if ((rc = alloc(&T, size_t(B) * ld[L] * es))) return rc;
+  H.assign(L, nullptr);
+  for (int l = 1; l < L; ++l)
+    if ((rc = alloc(&H[l], size_t(B) * ld[l] * es))) return rc;
+  dY.assign(L, nullptr);
+  for (int l = 0; l < L; ++l)
+    if ((rc = alloc(&dY[l], size_t(B) * ld[l + 1] * es))) return rc;
+  for (int k = 0; k < 2; ++k) {
+    W32[k].assign(L, nullptr);
+    Wbf[k].assign(L, nullptr);
+  }
+  for (int l = 0; l < L; ++l) {
+    const size_t n = size_t(dims[l + 1]) * ld[l];
+    if ((rc = alloc((void**)&W32[0][l], n * 4))) return rc;
+    if (!bf && (rc = alloc((void**)&W32[1][l], n * 4))) return rc;
+    if (bf) {
+      for (int k = 0; k < 2; ++k)
+        if ((rc = alloc((void**)&Wbf[k][l], n * 2))) return rc;
+    }
+  }
+  bias.assign(L, nullptr);
+  colsum.assign(L, nullptr);
+  for (int l = 0; l < L; ++l) {
+    if ((rc = alloc((void**)&bias[l], size_t(ld[l + 1]) * 4))) return rc;
+    if (has_bias && (rc = alloc((void**)&colsum[l], size_t(TM) * ld[l + 1] * 4))) return rc;
+  }
+  if ((rc = alloc((void**)&loss_partials, size_t(TM) * 64 * 4 + size_t(TM) * ((dims[L] + 15) / 16) * 4))) return rc;
+  if ((rc = alloc((void**)&losses, size_t(loss_cap) * 4))) return rc;
+  if ((rc = alloc((void**)&step_ctr, 16))) return rc;
+  if ((rc = alloc((void**)&Yout, size_t(B) * ld[L] * 4))) return rc;
+  if (grad_mode == 1) {
+    dW_off.resize(L);
+    db_off.resize(L);
+    long long o = 0;
+    for (int l = 0; l < L; ++l) {
+      dW_off[l] = o;
+      o += (long long)dims[l + 1] * ld[l];
+    }
+    for (int l = 0; l < L; ++l) {
+      db_off[l] = o;
+      o += round_up(dims[l + 1], 4);
+    }
+    grad_count = o;
+    if ((rc = alloc((void**)&grads, size_t(o) * 4))) return rc;
+  }
+  for (int l = 0; l < L; ++l) flops_per_step += 2.0 * B * dims[l] * dims[l + 1] * (l > 0 ? 3 : 2);
+  return PKT_OK;
+}
+
+// Registers the GEMMs of weight parity p and builds that parity's task lists.
+int Mlp::build(int p) {
+  const int cur = p, nxt = 1 - p;
+  std::vector<pkt_gemm_desc> g;
+  std::vector<int> fwd(L), dgr(L, -1), wgr(L);
+  // ---- forward
+  for (int l = 0; l < L; ++l) {
+    pkt_gemm_desc d{};
+    d.M = B;
+    d.N = dims[l + 1];
+    d.K = dims[l];
+    d.in_dtype = in_dtype();
+    d.a = Hin(l);
+    d.lda = ld[l];
+    d.a_major = PKT_MAJOR_K;
+    d.b = Wop(l, cur);
+    d.ldb = ld[l];
+    d.b_major = PKT_MAJOR_K;
+    d.bn = pick_bn(d.M, d.N, false);
+    d.bias = has_bias ? bias[l] : nullptr;
+    if (l < L - 1) {
+      d.epilogue = PKT_EPI_BIAS_ACT;
+      d.relu = 1;
+      d.out = H[l + 1];
+      d.ldo = ld[l + 1];
+      d.out_dtype = act_dtype();
+    } else {
+      d.epilogue = PKT_EPI_MSE;
+      d.relu = relu_last ? 1 : 0;
+      d.out = dY[L - 1];
+      d.ldo = ld[L];
+      d.out_dtype = act_dtype();
+      d.aux = T;
+      d.ldaux = ld[L];
+      d.scale = float(2.0 / (double(B) * double(dims[L])));
+      d.loss_partials = loss_partials;
+      d.colsum = has_bias ? colsum[L - 1] : nullptr;
+      d.ldcol = ld[L];
+      d.y_out = capture_y ? Yout : nullptr;
+      d.ldy = ld[L];
+    }
+    fwd[l] = int(g.size());
+    g.push_back(d);
+  }
+  // ---- dgrad (l >= 1) and wgrad
+  for (int l = L - 1; l >= 0; --l) {
+    if (l >= 1) {
+      pkt_gemm_desc d{};
+      d.M = B;
+      d.N = dims[l];
+      d.K = dims[l + 1];
+      d.in_dtype = in_dtype();
+      d.a = dY[l];
+      d.lda = ld[l + 1];
+      d.a_major = PKT_MAJOR_K;
+      d.b = Wop(l, cur);
+      d.ldb = ld[l];
+      d.b_major = PKT_MAJOR_MN;
+      d.bn = pick_bn(d.M, d.N, true);
+      d.epilogue = PKT_EPI_DGRAD_RELU;
+      d.out = dY[l - 1];
+      d.ldo = ld[l];
+      d.out_dtype = act_dtype();
+      d.aux = H[l];
+      d.ldaux = ld[l];
+      d.colsum = has_bias ? colsum[l - 1] : nullptr;
+      d.ldcol = ld[l];
+      dgr[l] = int(g.size());
+      g.push_back(d);
+    }
+    pkt_gemm_desc d{};
+    d.M = dims[l + 1];
+    d.N = dims[l];
+    d.K = B;
+    d.in_dtype = in_dtype();
+    d.a = dY[l];
+    d.lda = ld[l + 1];
+    d.a_major = PKT_MAJOR_MN;
+    d.b = Hin(l);
+    d.ldb = ld[l];
+    d.b_major = PKT_MAJOR_MN;
+    d.bn = pick_bn(d.M, d.N, true);
+    if (grad_mode == 0) {
+      d.epilogue = PKT_EPI_WGRAD_SGD;
+      d.w_in = Wmaster(l, cur);
+      d.w_out = Wmaster(l, nxt);
+      d.w_shadow = bf ? (void*)Wbf[nxt][l] : nullptr;
+      d.ldw = ld[l];
+      d.lr = lr;
+      d.out = nullptr;
+    } else {
+      d.epilogue = PKT_EPI_WGRAD_STORE;
+      d.out = grads + dW_off[l];
+      d.ldo = ld[l];
+      d.out_dtype = PKT_DTYPE_F32;
+    }
+    wgr[l] = int(g.size());
+    g.push_back(d);
+  }
+  int first = 0;
+  int rc = rt->register_gemms(g.data(), int(g.size()), &first);
+  if (rc) return rc;
+  auto G = [&](int idx) -> const DevGemm& { return rt->host_gemms[first + idx]; };
+
+  // ---- tokens
+  int next_id = 1;
+  std::vector<std::vector<int>> F(L, std::vector<int>(TM)), Bk(L, std::vector<int>(TM));
+  std::vector<int> BF(L);
+  for (int l = 0; l < L; ++l)
+    for (int i = 0; i < TM; ++i) F[l][i] = next_id++;
+  for (int l = 0; l < L - 1; ++l)
+    for (int i = 0; i < TM; ++i) Bk[l][i] = next_id++;
+  for (int i = 0; i < TM; ++i) Bk[L - 1][i] = F[L - 1][i];
+  for (int l = 0; l < L; ++l) BF[l] = next_id++;
+  const int WG_base = next_id;
+  next_id += L;
+  num_tokens = next_id;
+  if (num_tokens > 65535) return fail(PKT_ERR_UNSUPPORTED, "too many dependency tokens");
+  // marks per row block of dY_l (and total)
+  std::vector<int> dy_tn(L);
+  for (int l = 0; l < L; ++l) dy_tn[l] = (l == L - 1) ? G(fwd[L - 1]).tiles_n : G(dgr[l + 1]).tiles_n;
+
+  std::vector<pkt_task>& tl = tasks[p];
+  tl.clear();
+  auto gemm_task = [&](int gidx, int i, int j) {
+    pkt_task t{};
+    t.header.opcode = PKT_OP_GEMM;
+    pkt_gemm_tile_args a{uint32_t(first + gidx), uint32_t(i), uint32_t(j), 0};
+    t.header.arg_bytes = sizeof(a);
+    std::memcpy(t.args, &a, sizeof(a));
+    return t;
+  };
+  int tiles = 0;
+  for (int l = 0; l < L; ++l) {
+    const DevGemm& dg = G(fwd[l]);
+    for (int i = 0; i < TM; ++i)
+      for (int j = 0; j < dg.tiles_n; ++j) {
+        pkt_task t = gemm_task(fwd[l], i, j);
+        if (l > 0) {
+          t.header.buffer_read_id = uint16_t(F[l - 1][i]);
+          t.header.wait_count = uint32_t(G(fwd[l - 1]).tiles_n);
+        }
+        t.header.buffer_write_id = uint16_t(F[l][i]);
+        if (l == L - 1) t.header.ext_ids = uint32_t(BF[L - 1]) << 16;
+        tl.push_back(t);
+        ++tiles;
+      }
+  }
+  {
+    const DevGemm& dg = G(fwd[L - 1]);
+    pkt_task t{};
+    t.header.opcode = PKT_OP_LOSS_REDUCE;
+    pkt_loss_reduce_args a{loss_partials, losses, dg.tiles_m * dg.tiles_n,
+                           float(1.0 / (double(B) * double(dims[L]))), step_ctr};
+    t.header.arg_bytes = sizeof(a);
+    std::memcpy(t.args, &a, sizeof(a));
+    t.header.buffer_read_id = uint16_t(BF[L - 1]);
+    t.header.wait_count = uint32_t(TM * dg.tiles_n);
+    tl.push_back(t);
+  }
+  for (int l = L - 1; l >= 0; --l) {
+    if (l >= 1) {
+      const DevGemm& dg = G(dgr[l]);
+      for (int i = 0; i < TM; ++i)
+        for (int j = 0; j < dg.tiles_n; ++j) {
+          pkt_task t = gemm_task(dgr[l], i, j);
+          t.header.buffer_read_id = uint16_t(Bk[l][i]);
+          t.header.wait_count = uint32_t(dy_tn[l]);
+          t.header.buffer_write_id = uint16_t(Bk[l - 1][i]);
+          t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
+          tl.push_back(t);
+          ++tiles;
+        }
+    }
+    const DevGemm& wg = G(wgr[l]);
+    for (int i = 0; i < wg.tiles_m; ++i)
+      for (int j = 0; j < wg.tiles_n; ++j) {
+        pkt_task t = gemm_task(wgr[l], i, j);
+        t.header.buffer_read_id = uint16_t(BF[l]);
+        t.header.wait_count = uint32_t(TM * dy_tn[l]);
+        t.header.buffer_write_id = uint16_t(WG_base + l);
+        tl.push_back(t);
+        ++tiles;
+      }
+    if (has_bias) {
+      const int n = dims[l + 1];
+      for (int c0 = 0; c0 < n; c0 += 512) {
+        pkt_task t{};
+        t.header.opcode = PKT_OP_BIAS_SGD;
+        pkt_bias_sgd_args a{};
+        a.partials = colsum[l];
+        a.num_partials = TM;
+        a.ld = ld[l + 1];
+        a.col_begin = c0;
+        a.col_end = std::min(n, c0 + 512);
+        if (grad_mode == 0) {
+          a.bias = bias[l];
+          a.lr = lr;
+        } else {
+          a.grad_out = grads + db_off[l];
+        }
+        t.header.arg_bytes = sizeof(a);
+        std::memcpy(t.args, &a, sizeof(a));
+        t.header.buffer_read_id = uint16_t(BF[l]);
+        t.header.wait_count = uint32_t(TM * dy_tn[l]);
+        tl.push_back(t);
+      }
+    }
+  }
+  gemm_tiles_per_step = tiles;
+
+  // ---- separate update list (grad_mode 1): runs after the gradient all-reduce
+  std::vector<pkt_task>& ul = update[p];
+  ul.clear();
+  if (grad_mode == 1) {
+    const float lre = lr * grad_scale;
+    for (int l = 0; l < L; ++l) {
+      const long long n = (long long)dims[l + 1] * ld[l];
+      const long long chunk = 1 << 16;
+      for (long long o = 0; o < n; o += chunk) {
+        pkt_task t{};
+        t.header.opcode = PKT_OP_SGD_MIXED;
+        pkt_sgd_mixed_args a{};
+        a.w = Wmaster(l, cur) + o;
+        a.g = grads + dW_off[l] + o;
+        a.w_out = Wmaster(l, nxt) + o;
+        a.w_bf16 = bf ? Wbf[nxt][l] + o : nullptr;
+        a.n = std::min(chunk, n - o);
+        a.lr = lre;
+        t.header.arg_bytes = sizeof(a);
+        std::memcpy(t.args, &a, sizeof(a));
+        ul.push_back(t);
+      }
+      if (has_bias) {
+        pkt_task t{};
+        t.header.opcode = PKT_OP_BIAS_SGD;
+        pkt_bias_sgd_args a{};
+        a.partials = grads + db_off[l];
+        a.num_partials = 1;
+        a.ld = 0;
+        a.col_begin = 0;
+        a.col_end = dims[l + 1];
+        a.bias = bias[l];
+        a.lr = lre;
+        t.header.arg_bytes = sizeof(a);
+        std::memcpy(t.args, &a, sizeof(a));
+        ul.push_back(t);
+      }
+    }
+  }
+  // ---- device copies
+  cudaFree(d_tasks[p]);
+  cudaFree(d_update[p]);
+  d_tasks[p] = d_update[p] = nullptr;
+  cudaError_t e = cudaMalloc(&d_tasks[p], sizeof(pkt_task) * std::max<size_t>(1, tl.size()));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(step tasks)");
+  e = cudaMemcpy(d_tasks[p], tl.data(), sizeof(pkt_task) * tl.size(), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "copy step tasks");
+  if (!ul.empty()) {
+    e = cudaMalloc(&d_update[p], sizeof(pkt_task) * ul.size());
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(update tasks)");
+    e = cudaMemcpy(d_update[p], ul.data(), sizeof(pkt_task) * ul.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "copy update tasks");
+  }
+  return rt->ensure_tokens(num_tokens);
+}
+
+int Mlp::launch_list(pkt_task* d, int n, cudaStream_t st) {
+  rt->num_tokens = rt->token_cap;
+  cudaError_t e = cudaMemsetAsync(rt->d_state, 0, sizeof(int) * state_ints(rt->num_tokens), st);
+  if (e != cudaSuccess) return cuda_fail(e, "reset token state");
+  KParams kp{};
+  kp.tasks = d;
+  kp.num_tasks = n;
+  kp.num_tokens = rt->num_tokens;
+  kp.state = rt->d_state;
+  kp.gemms = rt->d_gemms;
+  kp.num_gemms = rt->num_gemms;
+  kp.chunk = 1;
+  kp.timeout_ns = rt->timeout_ns;
+  kp.perf = nullptr;
+  if (rt->perf_enabled) {
+    if (rt->perf_cap < rt->num_sms) {
+      cudaFree(rt->d_perf);
+      e = cudaMalloc(&rt->d_perf, sizeof(unsigned long long) * PKT_PERF_WORDS * rt->num_sms);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(perf)");
+      rt->perf_cap = rt->num_sms;
+    }
+    kp.perf = rt->d_perf;
+  }
+  rt->last_blocks = rt->num_sms;
+  e = launch_megakernel(kp, rt->num_sms, st);
+  if (e != cudaSuccess) return cuda_fail(e, "launch megakernel");
+  return PKT_OK;
+}
+
+}  // namespace pkb
+
+using pkb::Mlp;
+struct pkt_mlp {
+  Mlp* m;
+};
+
+static int rebuild(Mlp* m) {
+  m->rt->num_gemms = 0;
+  m->rt->host_gemms.clear();
+  int rc = m->build(0);
+  if (rc) return rc;
+  return m->build(1);
+}
+
+extern "C" {
+
+int pkt_mlp_create(int device, const pkt_mlp_config* cfg, pkt_mlp** out) {
+  if (!cfg || !out) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  pkb::Runtime* rt = nullptr;
+  int rc = pkb::Runtime::create(device, &rt);
+  if (rc) return rc;
+  Mlp* m = new Mlp();
+  m->rt = rt;
+  rc = m->setup(*cfg);
+  if (!rc) rc = rebuild(m);
+  if (rc) {
+    delete m;
+    return rc;
+  }
+  *out = new pkt_mlp{m};
+  return PKT_OK;
+}
+
+int pkt_mlp_destroy(pkt_mlp* h) {
+  if (!h) return PKT_OK;
+  delete h->m;
+  delete h;
+  return PKT_OK;
+}
+
+int pkt_mlp_set_params(pkt_mlp* h, const float* W, const float* b) {
+  if (!h || !W) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  cudaSetDevice(m->rt->device);
+  cudaDeviceSynchronize();
+  size_t wo = 0, bo = 0;
+  for (int l = 0; l < m->L; ++l) {
+    const int rows = m->dims[l + 1], cols = m->dims[l];
+    float* dst = m->Wmaster(l, m->parity);
+    cudaError_t e = cudaMemcpy2D(dst, size_t(m->ld[l]) * 4, W + wo, size_t(cols) * 4, size_t(cols) * 4, rows,
+                                 cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return pkb::cuda_fail(e, "copy weights");
+    if (m->bf) {
+      pkb::f32_to_bf16_2d<<<256, 256>>>(dst, rows, cols, m->ld[l], m->Wbf[m->parity][l], m->ld[l]);
+    }
+    wo += size_t(rows) * cols;
+    if (b) {
+      e = cudaMemcpy(m->bias[l], b + bo, size_t(rows) * 4, cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) return pkb::cuda_fail(e, "copy bias");
+    } else {
+      cudaMemset(m->bias[l], 0, size_t(rows) * 4);
+    }
+    bo += rows;
+  }
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return pkb::cuda_fail(e, "set params");
+  return PKT_OK;
+}
+
+int pkt_mlp_get_params(pkt_mlp* h, float* W, float* b) {
+  if (!h || !W) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  cudaSetDevice(m->rt->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return pkb::cuda_fail(e, "sync");
+  size_t wo = 0, bo = 0;
+  for (int l = 0; l < m->L; ++l) {
+    const int rows = m->dims[l + 1], cols = m->dims[l];
+    e = cudaMemcpy2D(W + wo, size_t(cols) * 4, m->Wmaster(l, m->parity), size_t(m->ld[l]) * 4, size_t(cols) * 4,
+                     rows, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return pkb::cuda_fail(e, "read weights");
+    wo += size_t(rows) * cols;
+    if (b) {
+      e = cudaMemcpy(b + bo, m->bias[l], size_t(rows) * 4, cudaMemcpyDeviceToHost);
+      if (e != cudaSuccess) return pkb::cuda_fail(e, "read bias");
+    }
+    bo += rows;
+  }
+  return PKT_OK;
+}
+
+int pkt_mlp_get_grads(pkt_mlp* h, float* dW, float* db) {
+  if (!h || !dW) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  if (m->grad_mode != 1) return pkb::fail(PKT_ERR_ARGS, "gradients are only stored with grad_mode 1");
+  cudaSetDevice(m->rt->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return pkb::cuda_fail(e, "sync");
+  size_t wo = 0, bo = 0;
+  for (int l = 0; l < m->L; ++l) {
+    const int rows = m->dims[l + 1], cols = m->dims[l];
+    e = cudaMemcpy2D(dW + wo, size_t(cols) * 4, m->grads + m->dW_off[l], size_t(m->ld[l]) * 4, size_t(cols) * 4,
+                     rows, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return pkb::cuda_fail(e, "read grads");
+    wo += size_t(rows) * cols;
+    if (db) {
+      e = cudaMemcpy(db + bo, m->grads + m->db_off[l], size_t(rows) * 4, cudaMemcpyDeviceToHost);
+      if (e != cudaSuccess) return pkb::cuda_fail(e, "read bias grads");
+    }
+    bo += rows;
+  }
+  return PKT_OK;
+}
+
+int pkt_mlp_load_batch(pkt_mlp* h, const void* x, const void* t, int on_device, void* stream) {
+  if (!h || !x || !t) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  cudaSetDevice(m->rt->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  cudaError_t e = cudaMemcpy2DAsync(m->X, size_t(m->ld[0]) * m->es, x, size_t(m->dims[0]) * m->es,
+                                    size_t(m->dims[0]) * m->es, m->B, kind, st);
+  if (e != cudaSuccess) return pkb::cuda_fail(e, "copy x");
+  e = cudaMemcpy2DAsync(m->T, size_t(m->ld[m->L]) * m->es, t, size_t(m->dims[m->L]) * m->es,
+                        size_t(m->dims[m->L]) * m->es, m->B, kind, st);
+  if (e != cudaSuccess) return pkb::cuda_fail(e, "copy target");
+  return PKT_OK;
+}
+
+int pkt_mlp_train(pkt_mlp* h, int steps, void* stream) {
+  if (!h || steps < 0) return pkb::fail(PKT_ERR_ARGS, "bad argument");
+  Mlp* m = h->m;
+  if (m->losses_enqueued + steps > m->loss_cap)
+    return pkb::fail(PKT_ERR_ARGS, "loss buffer full (%d steps); call pkt_mlp_reset_losses", m->loss_cap);
+  cudaSetDevice(m->rt->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int s = 0; s < steps; ++s) {
+    const int p = m->parity;
+    int rc = m->launch_list(m->d_tasks[p], int(m->tasks[p].size()), st);
+    if (rc) return rc;
+    if (m->grad_mode == 1) {
+      rc = m->launch_list(m->d_update[p], int(m->update[p].size()), st);
+      if (rc) return rc;
+    }
+    m->parity ^= 1;
+    m->losses_enqueued++;
+  }
+  return PKT_OK;
+}
+
+int pkt_mlp_forward_backward(pkt_mlp* h, void* stream) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  if (m->grad_mode != 1) return pkb::fail(PKT_ERR_ARGS, "forward_backward needs grad_mode 1");
+  if (m->losses_enqueued + 1 > m->loss_cap) return pkb::fail(PKT_ERR_ARGS, "loss buffer full");
+  cudaSetDevice(m->rt->device);
+  m->losses_enqueued++;
+  return m->launch_list(m->d_tasks[m->parity], int(m->tasks[m->parity].size()), static_cast<cudaStream_t>(stream));
+}
+
+int pkt_mlp_apply_update(pkt_mlp* h, void* stream) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  if (m->grad_mode != 1) return pkb::fail(PKT_ERR_ARGS, "apply_update needs grad_mode 1");
+  cudaSetDevice(m->rt->device);
+  const int p = m->parity;
+  int rc = m->launch_list(m->d_update[p], int(m->update[p].size()), static_cast<cudaStream_t>(stream));
+  if (rc) return rc;
+  m->parity ^= 1;
+  return PKT_OK;
+}
+
+int pkt_mlp_grad_buffer(pkt_mlp* h, float** ptr, long long* count) {
+  if (!h || !ptr || !count) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  if (h->m->grad_mode != 1) return pkb::fail(PKT_ERR_ARGS, "gradient buffer exists with grad_mode 1 only");
+  *ptr = h->m->grads;
+  *count = h->m->grad_count;
+  return PKT_OK;
+}
+
+int pkt_mlp_set_grad_scale(pkt_mlp* h, float scale) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  cudaSetDevice(h->m->rt->device);
+  cudaDeviceSynchronize();
+  h->m->grad_scale = scale;
+  return rebuild(h->m);
+}
+
+int pkt_mlp_set_output_capture(pkt_mlp* h, int enabled) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  cudaSetDevice(h->m->rt->device);
+  cudaDeviceSynchronize();
+  h->m->capture_y = enabled != 0;
+  return rebuild(h->m);
+}
+
+int pkt_mlp_losses(pkt_mlp* h, float* out, int max_n, int* n) {
+  if (!h || !out || !n) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  cudaSetDevice(m->rt->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return pkb::cuda_fail(e, "sync");
+  const int k = std::min(max_n, m->losses_enqueued);
+  if (k > 0) {
+    e = cudaMemcpy(out, m->losses, sizeof(float) * k, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return pkb::cuda_fail(e, "read losses");
+  }
+  *n = k;
+  return PKT_OK;
+}
+
+int pkt_mlp_reset_losses(pkt_mlp* h) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  cudaSetDevice(m->rt->device);
+  cudaDeviceSynchronize();
+  cudaMemset(m->step_ctr, 0, 16);
+  m->losses_enqueued = 0;
+  return PKT_OK;
+}
+
+int pkt_mlp_loss_ptr(pkt_mlp* h, int i, float** out) {
+  if (!h || !out || i < 0 || i >= h->m->loss_cap) return pkb::fail(PKT_ERR_ARGS, "bad argument");
+  *out = h->m->losses + i;
+  return PKT_OK;
+}
+
+int pkt_mlp_get_output(pkt_mlp* h, float* y) {
+  if (!h || !y) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  if (!m->capture_y) return pkb::fail(PKT_ERR_ARGS, "output capture is off (pkt_mlp_set_output_capture)");
+  cudaSetDevice(m->rt->device);
+  cudaError_t e = cudaMemcpy2D(y, size_t(m->dims[m->L]) * 4, m->Yout, size_t(m->ld[m->L]) * 4,
+                               size_t(m->dims[m->L]) * 4, m->B, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return pkb::cuda_fail(e, "read output");
+  return PKT_OK;
+}
+
+int pkt_mlp_status(pkt_mlp* h, int* code, int* task_index, int* detail) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  return h->m->rt->status(code, task_index, detail);
+}
+
+int pkt_mlp_step_info(pkt_mlp* h, int* tasks, int* gemm_tiles, double* flops) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  if (tasks) *tasks = int(h->m->tasks[0].size() + h->m->update[0].size());
+  if (gemm_tiles) *gemm_tiles = h->m->gemm_tiles_per_step;
+  if (flops) *flops = h->m->flops_per_step;
+  return PKT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,53 @@
+// Host-side runtime object behind pkt_runtime (C-ABI) and the MLP engine.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "internal.h"
+
+namespace pkb {
+
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+int gemm_tiles(const pkt_gemm_desc& d, int* tm, int* tn);
+int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g);
+
+struct Runtime {
+  int device = -1;
+  int num_sms = 0;
+  pkt_task* d_tasks = nullptr;
+  int max_tasks = 0;
+  int num_tasks = 0;
+  int* d_state = nullptr;
+  int token_cap = 0;
+  int num_tokens = 256;
+  DevGemm* d_gemms = nullptr;
+  int num_gemms = 0;
+  int gemm_cap = 0;
+  std::vector<DevGemm> host_gemms;
+  unsigned long long* d_counter = nullptr;
+  bool accounting = false;
+  bool perf_enabled = false;
+  unsigned long long* d_perf = nullptr;
+  int perf_cap = 0;
+  int last_blocks = 0;
+  unsigned long long timeout_ns = 2000000000ull;
+  std::vector<int> segments;
+  int segment_window = 4;
+
+  ~Runtime();
+  static int create(int dev, Runtime** out);
+  void release();
+  int initialize(int max_tasks);
+  int ensure_tokens(int need);
+  static int scan_tokens(const pkt_task* tasks, int n);
+  int submit_async(const pkt_task* tasks, int n, cudaStream_t stream, bool sync_copy);
+  int reset_state(cudaStream_t stream, bool sync);
+  int launch(int blocks, cudaStream_t stream);
+  int status(int* code, int* task, int* detail);
+  int register_gemms(const pkt_gemm_desc* descs, int n, int* first);
+};
+
+}  // namespace pkb
