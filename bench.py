@@ -1,0 +1,388 @@
+"""Benchmark of the pkt MLP training step on B200 (see DESIGN.md for the method).
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg2]
+
+Default workload (N=1): the 4-layer ReLU MLP 1024->4096->4096->4096->1024, bf16
+weights/activations with fp32 accumulation and fp32 master weights, batch 8192,
+MSE, SGD lr=1e-3 (the configuration the headline metric is quoted on). N>1:
+data parallel, the same model with 8192 rows per GPU (weak scaling), fp32
+gradients all-reduced with NCCL between the backward and the update launch.
+One JSON line on rank 0.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "cfg1": dict(dims=[128, 64], batch=256, dtype="tf32", lr=1e-2,
+                 desc="train_linear: Linear 128->64, fp32/TF32, batch 256, bias, MSE, SGD lr=1e-2"),
+    "cfg2": dict(dims=[1024, 4096, 4096, 4096, 1024], batch=8192, dtype="bf16", lr=1e-3,
+                 desc="4-layer ReLU MLP 1024->4096->4096->4096->1024, bf16 weights/activations, "
+                      "fp32 accumulate, fp32 master weights, batch 8192/GPU, MSE, SGD lr=1e-3"),
+    "cfg3": dict(dims=[512] * 17, batch=2048, dtype="bf16", lr=1e-3,
+                 desc="deep narrow MLP: 16 layers of width 512, ReLU, bf16/fp32-acc, batch 2048"),
+    "cfg4": dict(dims=[8192] * 9, batch=8192, dtype="bf16", lr=1e-4,
+                 desc="wide MLP: 8 layers of width 8192, ReLU, bf16/fp32-acc, batch 8192/GPU"),
+    "cfg5": dict(dims=[1000, 3000, 777, 10], batch=4099, dtype="tf32", lr=5e-3,
+                 desc="ragged MLP 1000->3000->777->10, fp32 storage with TF32 tensor cores, batch 4099"),
+}
+
+
+def flops_per_sample(dims):
+    return sum(2.0 * dims[l] * dims[l + 1] * (3 if l > 0 else 2) for l in range(len(dims) - 1))
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=5)
+        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(cfg, rank, seed=1234):
+    rng = np.random.default_rng(seed + rank)
+    dims, B = cfg["dims"], cfg["batch"]
+    x = rng.standard_normal((B, dims[0]), dtype=np.float32)
+    if cfg is CONFIGS["cfg5"]:
+        x = rng.uniform(-3, 3, (B, dims[0])).astype(np.float32)
+        t = np.zeros((B, dims[-1]), np.float32)
+        t[np.arange(B), rng.integers(0, dims[-1], B)] = 1.0
+    else:
+        t = rng.standard_normal((B, dims[-1]), dtype=np.float32)
+    # Kaiming-uniform weights (bound sqrt(6/fan_in)), zero bias
+    Ws = [(rng.uniform(-1, 1, (dims[l + 1], dims[l])) * np.sqrt(6.0 / dims[l])).astype(np.float32)
+          for l in range(len(dims) - 1)]
+    bs = [np.zeros(dims[l + 1], np.float32) for l in range(len(dims) - 1)]
+    return x, t, Ws, bs
+
+
+def cpu_sample_rate(cfg, rows, threads=0):
+    """The oracle (CPU restatement of pkt's host training loop, extended to the
+    MLP) timed on the box's host cores on two row counts of the same workload
+    (rows and 2*rows); one step = fixed part (weight rounding, SGD) + rows x
+    per-row part, extrapolated to the full batch. Returns (samples/s, threads,
+    seconds timed, description)."""
+    from oracle import oracle as orc
+    if threads:
+        orc.lib().orc_set_num_threads(threads)
+    nthreads = orc.lib().orc_num_threads()
+    B = cfg["batch"]
+    r1 = max(4, min(rows, B // 2))
+    r2 = 2 * r1
+    x, t, Ws, bs = make_inputs(dict(cfg, batch=r2), 0, seed=99)
+    mode = cfg["dtype"]
+    times = []
+    for r in (r1, r2):
+        t0 = time.perf_counter()
+        orc.mlp_train(cfg["dims"], x[:r], t[:r], Ws, bs, cfg["lr"], 1, mode=mode)
+        times.append(time.perf_counter() - t0)
+    per_row = max((times[1] - times[0]) / (r2 - r1), 1e-12)
+    fixed = max(times[0] - r1 * per_row, 0.0)
+    step_s = fixed + B * per_row
+    desc = (f"oracle step on {r1} and {r2} rows ({times[0]:.2f} s, {times[1]:.2f} s), "
+            f"extrapolated to the {B}-row batch: {fixed:.2f} s fixed + {per_row * 1e3:.2f} ms/row")
+    return B / step_s, nthreads, sum(times), desc
+
+
+def cpu_rows(cfg):
+    # about 5 s of single-step oracle work at the smaller row count on ~16 cores
+    return int(max(4, min(cfg["batch"] // 2, 5e10 / flops_per_sample(cfg["dims"]))))
+
+
+def init_dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def run_reference(args, cfg_name, cfg):
+    ws, rank, _ = init_dist()
+    if rank != 0:
+        return
+    # bounded sample per step: rows chosen so one step is ~1-3 s of CPU work
+    rows = cpu_rows(cfg)
+    rates = []
+    thr = 0
+    secs = 0.0
+    desc = ""
+    for i in range(min(args.warmup, 1) + max(args.steps, 1)):
+        r, thr, dt, desc = cpu_sample_rate(cfg, rows)
+        if i >= args.warmup:
+            rates.append(r)
+            secs += dt
+        if secs > 60:
+            break
+    v = float(np.mean(rates))
+    line = {
+        "impl": "reference", "metric": "MLP train samples/s & % dense BF16 TC peak at 1/2/4/8 B200",
+        "value": v, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * cfg["batch"] / v,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,1) inputs/targets, Kaiming-uniform weights)",
+        "config": {"workload": cfg_name + ": " + cfg["desc"], "global_batch": cfg["batch"],
+                   "parallelism": "host CPU, OpenMP"},
+        "cpu_baseline": {"value": v, "unit": "samples/s", "cores": thr, "kind": "port",
+                         "sample": desc + f"; {len(rates)} timed repetitions, {secs:.1f} s"},
+        "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, cfg_name, cfg):
+    import torch
+    ws, rank, local = init_dist()
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    import pkt_b200
+    from pkt_b200.mlp import to_bf16_bits
+
+    dims, B = cfg["dims"], cfg["batch"]
+    grad_mode = 1 if ws > 1 else 0
+    eng = pkt_b200.MLP(dims, B, dtype=cfg["dtype"], lr=cfg["lr"], bias=True, grad_mode=grad_mode,
+                       device=local)
+    if ws > 1:
+        eng.set_grad_scale(1.0 / ws)
+    x, t, Ws, bs = make_inputs(cfg, 0)  # same initial weights on every rank
+    eng.set_params(Ws, bs)
+    xs, ts = make_inputs(cfg, rank)[:2]  # per-rank data shard
+    # two distinct pinned host batches, in the engine's storage type
+    host_x, host_t = [], []
+    for k in range(2):
+        xa = eng.storage_array(np.roll(xs, k, axis=0))
+        ta = eng.storage_array(np.roll(ts, k, axis=0))
+        hx = torch.from_numpy(xa.view(np.int16) if xa.dtype == np.uint16 else xa).pin_memory()
+        ht = torch.from_numpy(ta.view(np.int16) if ta.dtype == np.uint16 else ta).pin_memory()
+        host_x.append(hx)
+        host_t.append(ht)
+    h2d_bytes = host_x[0].numel() * host_x[0].element_size() + host_t[0].numel() * host_t[0].element_size()
+
+    stream = torch.cuda.Stream()
+    copy_stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    grad_t = None
+    if ws > 1:
+        gptr, gcount = eng.grad_buffer()
+        grad_t = _wrap_device_f32(gptr, gcount, local)
+
+    def step(s_ptr):
+        if ws > 1:
+            eng.forward_backward(s_ptr)
+            with torch.cuda.stream(stream):
+                dist.all_reduce(grad_t)
+            eng.apply_update(s_ptr)
+        else:
+            eng.train(1, s_ptr)
+
+    launches_per_step = 2 if ws > 1 else 1
+    # ---------------- device-resident timing
+    eng.load_batch_ptr(host_x[0].data_ptr(), host_t[0].data_ptr(), 0, sp)
+    for _ in range(args.warmup):
+        step(sp)
+    torch.cuda.synchronize()
+    eng.reset_losses()
+    peaks, peak_kind = measured_peaks()
+    sampler = ClockSampler(local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    wall0 = time.perf_counter()
+    evs[0].record(stream)
+    for i in range(args.steps):
+        step(sp)
+        evs[i + 1].record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop()
+    t_ms = evs[0].elapsed_time(evs[-1])
+    per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    losses = eng.losses()
+    if dist:
+        tt = torch.tensor([t_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_ms = float(tt.item())
+    ms_per_step = t_ms / args.steps
+    value = ws * B * args.steps / (t_ms / 1e3)
+    F = flops_per_sample(dims) * B
+    tflops = F / (ms_per_step / 1e3) / 1e12
+    # per-launch kernel time (grad_mode 0: one launch per step) -> roofline of the megakernel
+    kern_ms = float(np.median(per_step)) if ws == 1 else ms_per_step
+    achieved = F / (kern_ms / 1e3) / 1e12
+    peak = peaks.get("bf16_tflops_sustained", 1369.1)
+    burst = peaks.get("bf16_tflops", 1646.1)
+
+    # ---------------- end-to-end through the public API with host buffers
+    eng.reset_losses()
+    loss_host = torch.zeros(args.steps, dtype=torch.float32).pin_memory()
+    done_ev = [torch.cuda.Event() for _ in range(args.steps)]
+    copy_ev = [torch.cuda.Event() for _ in range(args.steps + 1)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(copy_stream)
+    stream.wait_stream(copy_stream)
+    cs = copy_stream.cuda_stream
+    eng.load_batch_ptr(host_x[0].data_ptr(), host_t[0].data_ptr(), 0, cs)
+    copy_ev[0].record(copy_stream)
+    for i in range(args.steps):
+        stream.wait_event(copy_ev[i])
+        step(sp)
+        done_ev[i].record(stream)
+        # next batch into the other slot once the step that last read it (i-1) is done
+        if i + 1 < args.steps:
+            if i >= 1:
+                copy_stream.wait_event(done_ev[i - 1])
+            k = (i + 1) % 2
+            eng.load_batch_ptr(host_x[k].data_ptr(), host_t[k].data_ptr(), 0, cs)
+            copy_ev[i + 1].record(copy_stream)
+        # device -> host read of this step's loss
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(done_ev[i])
+            lp = eng.loss_ptr(i)
+            loss_host[i:i + 1].copy_(_wrap_device_f32(lp, 1, local), non_blocking=True)
+    copy_stream.wait_stream(stream)
+    e1.record(copy_stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        tt = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e_value = ws * B * args.steps / (e2e_ms / 1e3)
+    e2e_losses = loss_host.numpy().copy()
+    code = eng.status()[0]
+
+    if rank != 0:
+        return
+    line = {
+        "metric": "MLP train samples/s & % dense BF16 TC peak at 1/2/4/8 B200",
+        "value": value, "unit": "samples/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": "synthetic (seeded N(0,1) inputs/targets, Kaiming-uniform weights, zero bias)",
+        "config": {"workload": cfg_name + ": " + cfg["desc"], "global_batch": B * ws,
+                   "per_gpu_batch": B, "parallelism": f"dp{ws}" if ws > 1 else "single GPU",
+                   "l2": "no flush: every step streams > 126 MB (weights, activations, gradients "
+                         "exceed L2)", "launches_per_step": launches_per_step},
+        "tflops": tflops, "pct_peak_measured_sustained": 100.0 * tflops / peak,
+        "pct_peak_measured_burst": 100.0 * tflops / burst,
+        "pct_peak_spec_2250": 100.0 * tflops / 2250.0,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "peak_kind": f"{peak_kind} bf16_tflops_sustained (kernel timed back to back "
+                                  f"for the whole run)",
+                     "kernel": "pk_megakernel (one launch = one training step)"},
+        "e2e": {"value": e2e_value, "unit": "samples/s", "h2d_bytes_per_step": h2d_bytes,
+                "d2h_bytes_per_step": 4,
+                "method": "pkt_mlp_load_batch from pinned host memory (copy stream, next batch "
+                          "overlapping the current step) + pkt_mlp_train + D2H loss read, every step"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "loss_first_last": [float(losses[0]), float(losses[-1])] if len(losses) else None,
+        "e2e_loss_last": float(e2e_losses[-1]),
+        "device_status": code,
+        "wall_s_timed": wall,
+    }
+    if ws == 1 and not args.no_cpu:
+        r, thr, dt, desc = cpu_sample_rate(cfg, cpu_rows(cfg))
+        line["cpu_baseline"] = {"value": r, "unit": "samples/s", "cores": thr, "kind": "port",
+                                "sample": desc}
+    print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+def _wrap_device_f32(ptr, count, device):
+    import torch
+
+    class _CAI:
+        def __init__(self):
+            self.__cuda_array_interface__ = {"shape": (count,), "typestr": "<f4",
+                                             "data": (ptr, False), "version": 3, "strides": None}
+    return torch.as_tensor(_CAI(), device=torch.device("cuda", device))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, args.config, cfg)
+    else:
+        run_ours(args, args.config, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -224,7 +224,11 @@ int pkt_mlp_get_params(pkt_mlp* m, float* W, float* b);
 int pkt_mlp_get_grads(pkt_mlp* m, float* dW, float* db);
 /* Batch upload: x [batch, d0], target [batch, dL], host or device memory, in the
  * engine's storage type (uint16 bf16 bits for PKT_DTYPE_BF16, fp32 for TF32).
- * Stream-ordered (host memory should be pinned for async copies). */
+ * Stream-ordered (host memory should be pinned for async copies). The engine
+ * has two input slots: each call fills the slot the previous call did not use
+ * and makes it the one later training steps read, so a copy on another stream
+ * can overlap the step still reading the other slot (the caller orders the
+ * copy after the step that last read its slot, two loads back). */
 int pkt_mlp_load_batch(pkt_mlp* m, const void* x, const void* target, int on_device, void* stream);
 /* Enqueue `steps` training steps on the loaded batch. */
 int pkt_mlp_train(pkt_mlp* m, int steps, void* stream);

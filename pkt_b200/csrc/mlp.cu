@@ -60,8 +60,12 @@ struct Mlp {
   float grad_scale = 1.0f;
   bool capture_y = false;
 
-  void* X = nullptr;
-  void* T = nullptr;
+  // Two input slots (x, target): pkt_mlp_load_batch fills the idle slot and makes it
+  // the active one, so the copy of the next batch can overlap the current step.
+  void* Xs[2] = {nullptr, nullptr};
+  void* Ts[2] = {nullptr, nullptr};
+  int active_slot = 0;
+  int next_slot = 0;
   std::vector<void*> H;   // H[l], l = 1..L-1 (index 0 unused)
   std::vector<void*> dY;  // dY[l], l = 0..L-1
   std::vector<float*> W32[2];
@@ -80,8 +84,9 @@ struct Mlp {
 
   int parity = 0;
   int TM = 0;
-  std::vector<pkt_task> tasks[2], update[2];
-  pkt_task* d_tasks[2] = {nullptr, nullptr};
+  // step task lists by [weight parity][input slot]; update lists by weight parity
+  std::vector<pkt_task> tasks[2][2], update[2];
+  pkt_task* d_tasks[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
   pkt_task* d_update[2] = {nullptr, nullptr};
   int num_tokens = 0;
   int gemm_tiles_per_step = 0;
@@ -90,14 +95,17 @@ struct Mlp {
   ~Mlp() {
     if (rt) cudaSetDevice(rt->device);
     auto F = [](void* p) { cudaFree(p); };
-    F(X);
-    F(T);
+    for (int k = 0; k < 2; ++k) {
+      F(Xs[k]);
+      F(Ts[k]);
+      F(d_tasks[k][0]);
+      F(d_tasks[k][1]);
+    }
     for (auto p : H) F(p);
     for (auto p : dY) F(p);
     for (int k = 0; k < 2; ++k) {
       for (auto p : W32[k]) F(p);
       for (auto p : Wbf[k]) F(p);
-      F(d_tasks[k]);
       F(d_update[k]);
     }
     for (auto p : bias) F(p);
@@ -112,7 +120,7 @@ struct Mlp {
 
   int act_dtype() const { return bf ? PKT_DTYPE_BF16 : PKT_DTYPE_F32; }
   int in_dtype() const { return bf ? PKT_DTYPE_BF16 : PKT_DTYPE_TF32; }
-  const void* Hin(int l) const { return l == 0 ? X : H[l]; }
+  const void* Hin(int l, int q) const { return l == 0 ? Xs[q] : H[l]; }
   // weight copy the GEMMs of parity p read
   const void* Wop(int l, int p) const { return bf ? (const void*)Wbf[p][l] : (const void*)W32[p][l]; }
   float* Wmaster(int l, int p) const { return bf ? W32[0][l] : W32[p][l]; }
@@ -141,7 +149,7 @@ struct Mlp {
   }
 
   int setup(const pkt_mlp_config& c);
-  int build(int p);
+  int build(int p, int q);
   int launch_list(pkt_task* d, int n, cudaStream_t st);
 };
 
@@ -165,8 +173,10 @@ int Mlp::setup(const pkt_mlp_config& c) {
   for (int l = 0; l <= L; ++l) ld[l] = round_up(dims[l], 64);
   TM = (B + kBM - 1) / kBM;
   int rc;
-  if ((rc = alloc(&X, size_t(B) * ld[0] * es))) return rc;
-  if ((rc = alloc(&T, size_t(B) * ld[L] * es))) return rc;
+  for (int k = 0; k < 2; ++k) {
+    if ((rc = alloc(&Xs[k], size_t(B) * ld[0] * es))) return rc;
+    if ((rc = alloc(&Ts[k], size_t(B) * ld[L] * es))) return rc;
+  }
   H.assign(L, nullptr);
   for (int l = 1; l < L; ++l)
     if ((rc = alloc(&H[l], size_t(B) * ld[l] * es))) return rc;
@@ -215,8 +225,8 @@ int Mlp::setup(const pkt_mlp_config& c) {
   return PKT_OK;
 }
 
-// Registers the GEMMs of weight parity p and builds that parity's task lists.
-int Mlp::build(int p) {
+// Registers the GEMMs of weight parity p and input slot q and builds their task lists.
+int Mlp::build(int p, int q) {
   const int cur = p, nxt = 1 - p;
   std::vector<pkt_gemm_desc> g;
   std::vector<int> fwd(L), dgr(L, -1), wgr(L);
@@ -227,7 +237,7 @@ int Mlp::build(int p) {
     d.N = dims[l + 1];
     d.K = dims[l];
     d.in_dtype = in_dtype();
-    d.a = Hin(l);
+    d.a = Hin(l, q);
     d.lda = ld[l];
     d.a_major = PKT_MAJOR_K;
     d.b = Wop(l, cur);
@@ -247,7 +257,7 @@ int Mlp::build(int p) {
       d.out = dY[L - 1];
       d.ldo = ld[L];
       d.out_dtype = act_dtype();
-      d.aux = T;
+      d.aux = Ts[q];
       d.ldaux = ld[L];
       d.scale = float(2.0 / (double(B) * double(dims[L])));
       d.loss_partials = loss_partials;
@@ -293,7 +303,7 @@ int Mlp::build(int p) {
     d.a = dY[l];
     d.lda = ld[l + 1];
     d.a_major = PKT_MAJOR_MN;
-    d.b = Hin(l);
+    d.b = Hin(l, q);
     d.ldb = ld[l];
     d.b_major = PKT_MAJOR_MN;
     d.bn = pick_bn(d.M, d.N, true);
@@ -337,7 +347,7 @@ int Mlp::build(int p) {
   std::vector<int> dy_tn(L);
   for (int l = 0; l < L; ++l) dy_tn[l] = (l == L - 1) ? G(fwd[L - 1]).tiles_n : G(dgr[l + 1]).tiles_n;
 
-  std::vector<pkt_task>& tl = tasks[p];
+  std::vector<pkt_task>& tl = tasks[p][q];
   tl.clear();
   auto gemm_task = [&](int gidx, int i, int j) {
     pkt_task t{};
@@ -466,12 +476,12 @@ int Mlp::build(int p) {
     }
   }
   // ---- device copies
-  cudaFree(d_tasks[p]);
+  cudaFree(d_tasks[p][q]);
   cudaFree(d_update[p]);
-  d_tasks[p] = d_update[p] = nullptr;
-  cudaError_t e = cudaMalloc(&d_tasks[p], sizeof(pkt_task) * std::max<size_t>(1, tl.size()));
+  d_tasks[p][q] = d_update[p] = nullptr;
+  cudaError_t e = cudaMalloc(&d_tasks[p][q], sizeof(pkt_task) * std::max<size_t>(1, tl.size()));
   if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(step tasks)");
-  e = cudaMemcpy(d_tasks[p], tl.data(), sizeof(pkt_task) * tl.size(), cudaMemcpyHostToDevice);
+  e = cudaMemcpy(d_tasks[p][q], tl.data(), sizeof(pkt_task) * tl.size(), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return cuda_fail(e, "copy step tasks");
   if (!ul.empty()) {
     e = cudaMalloc(&d_update[p], sizeof(pkt_task) * ul.size());
@@ -521,9 +531,12 @@ struct pkt_mlp {
 static int rebuild(Mlp* m) {
   m->rt->num_gemms = 0;
   m->rt->host_gemms.clear();
-  int rc = m->build(0);
-  if (rc) return rc;
-  return m->build(1);
+  for (int p = 0; p < 2; ++p)
+    for (int q = 0; q < 2; ++q) {
+      int rc = m->build(p, q);
+      if (rc) return rc;
+    }
+  return PKT_OK;
 }
 
 extern "C" {
@@ -632,12 +645,15 @@ int pkt_mlp_load_batch(pkt_mlp* h, const void* x, const void* t, int on_device, 
   cudaSetDevice(m->rt->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-  cudaError_t e = cudaMemcpy2DAsync(m->X, size_t(m->ld[0]) * m->es, x, size_t(m->dims[0]) * m->es,
+  const int q = m->next_slot;
+  cudaError_t e = cudaMemcpy2DAsync(m->Xs[q], size_t(m->ld[0]) * m->es, x, size_t(m->dims[0]) * m->es,
                                     size_t(m->dims[0]) * m->es, m->B, kind, st);
   if (e != cudaSuccess) return pkb::cuda_fail(e, "copy x");
-  e = cudaMemcpy2DAsync(m->T, size_t(m->ld[m->L]) * m->es, t, size_t(m->dims[m->L]) * m->es,
+  e = cudaMemcpy2DAsync(m->Ts[q], size_t(m->ld[m->L]) * m->es, t, size_t(m->dims[m->L]) * m->es,
                         size_t(m->dims[m->L]) * m->es, m->B, kind, st);
   if (e != cudaSuccess) return pkb::cuda_fail(e, "copy target");
+  m->active_slot = q;
+  m->next_slot = q ^ 1;
   return PKT_OK;
 }
 
@@ -649,8 +665,8 @@ int pkt_mlp_train(pkt_mlp* h, int steps, void* stream) {
   cudaSetDevice(m->rt->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int s = 0; s < steps; ++s) {
-    const int p = m->parity;
-    int rc = m->launch_list(m->d_tasks[p], int(m->tasks[p].size()), st);
+    const int p = m->parity, q = m->active_slot;
+    int rc = m->launch_list(m->d_tasks[p][q], int(m->tasks[p][q].size()), st);
     if (rc) return rc;
     if (m->grad_mode == 1) {
       rc = m->launch_list(m->d_update[p], int(m->update[p].size()), st);
@@ -669,7 +685,8 @@ int pkt_mlp_forward_backward(pkt_mlp* h, void* stream) {
   if (m->losses_enqueued + 1 > m->loss_cap) return pkb::fail(PKT_ERR_ARGS, "loss buffer full");
   cudaSetDevice(m->rt->device);
   m->losses_enqueued++;
-  return m->launch_list(m->d_tasks[m->parity], int(m->tasks[m->parity].size()), static_cast<cudaStream_t>(stream));
+  const int p = m->parity, q = m->active_slot;
+  return m->launch_list(m->d_tasks[p][q], int(m->tasks[p][q].size()), static_cast<cudaStream_t>(stream));
 }
 
 int pkt_mlp_apply_update(pkt_mlp* h, void* stream) {
@@ -757,7 +774,7 @@ int pkt_mlp_status(pkt_mlp* h, int* code, int* task_index, int* detail) {
 
 int pkt_mlp_step_info(pkt_mlp* h, int* tasks, int* gemm_tiles, double* flops) {
   if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
-  if (tasks) *tasks = int(h->m->tasks[0].size() + h->m->update[0].size());
+  if (tasks) *tasks = int(h->m->tasks[0][0].size() + h->m->update[0].size());
   if (gemm_tiles) *gemm_tiles = h->m->gemm_tiles_per_step;
   if (flops) *flops = h->m->flops_per_step;
   return PKT_OK;
