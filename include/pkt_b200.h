@@ -157,6 +157,9 @@ typedef struct pkt_gemm_desc {
   float lr;
   void* y_out;       /* MSE: optional fp32 copy of y = acc + bias */
   int ldy;
+  int cta_pair;      /* 0/1: one CTA per 128 x bn tile; 2: a CTA pair per 256 x bn tile
+                        (tcgen05 cta_group::2, each CTA loads its A rows and half of B);
+                        must match the launch mode (pkt_runtime_set_cta_pair) */
 } pkt_gemm_desc;
 
 /* ---- runtime (pk::Runtime's C half) ------------------------------------ */
@@ -185,6 +188,9 @@ int pkt_runtime_clear_gemms(pkt_runtime* rt);
 int pkt_gemm_tiles(const pkt_gemm_desc* d, int* tiles_m, int* tiles_n);
 /* Wait budget of every device-side spin, in nanoseconds (default 2e9). */
 int pkt_runtime_set_timeout_ns(pkt_runtime* rt, unsigned long long ns);
+/* Launch mode: 1 = one CTA per SM works alone (default); 2 = CTA pairs (clusters of
+ * two SMs) share 256-row GEMM tiles; the block count is rounded up to even. */
+int pkt_runtime_set_cta_pair(pkt_runtime* rt, int pair);
 int pkt_runtime_set_task_accounting(pkt_runtime* rt, int enabled);
 int pkt_runtime_fetch_task_counter(pkt_runtime* rt, unsigned long long* out);
 int pkt_runtime_set_perf(pkt_runtime* rt, int enabled);
@@ -213,6 +219,8 @@ typedef struct pkt_mlp_config {
   int grad_mode;    /* 0: SGD fused into the weight-gradient epilogue; 1: store fp32
                        gradients, separate SGD pass (data parallel / inspection) */
   int max_bn;       /* largest tile N to use (0: 256) */
+  int cta_pair;     /* 0 or 2: CTA pairs share 256-row tiles (tcgen05 cta_group::2);
+                       1: every CTA computes its own 128-row tiles */
 } pkt_mlp_config;
 
 int pkt_mlp_create(int device, const pkt_mlp_config* cfg, pkt_mlp** out);
@@ -252,6 +260,9 @@ int pkt_mlp_grad_buffer(pkt_mlp* m, float** ptr, long long* count);
 int pkt_mlp_set_grad_scale(pkt_mlp* m, float scale);
 int pkt_mlp_forward_backward(pkt_mlp* m, void* stream);
 int pkt_mlp_apply_update(pkt_mlp* m, void* stream);
+/* Per-CTA role cycle counters of the last launch (same layout as pkt_runtime_fetch_perf). */
+int pkt_mlp_set_perf(pkt_mlp* m, int enabled);
+int pkt_mlp_fetch_perf(pkt_mlp* m, unsigned long long* out, int max_blocks, int* blocks);
 
 #ifdef __cplusplus
 }

@@ -48,13 +48,14 @@ class GemmDesc(ctypes.Structure):
                 ("relu", c_int), ("bias", c_void_p), ("aux", c_void_p), ("ldaux", c_int),
                 ("scale", c_float), ("loss_partials", c_void_p), ("colsum", c_void_p),
                 ("ldcol", c_int), ("w_in", c_void_p), ("w_out", c_void_p), ("w_shadow", c_void_p),
-                ("ldw", c_int), ("lr", c_float), ("y_out", c_void_p), ("ldy", c_int)]
+                ("ldw", c_int), ("lr", c_float), ("y_out", c_void_p), ("ldy", c_int),
+                ("cta_pair", c_int)]
 
 
 class MlpConfig(ctypes.Structure):
     _fields_ = [("num_layers", c_int), ("dims", ctypes.POINTER(c_int)), ("batch", c_int),
                 ("dtype", c_int), ("has_bias", c_int), ("relu_last", c_int), ("lr", c_float),
-                ("grad_mode", c_int), ("max_bn", c_int)]
+                ("grad_mode", c_int), ("max_bn", c_int), ("cta_pair", c_int)]
 
 
 _P = c_void_p
@@ -76,6 +77,7 @@ _SIGS = {
     "pkt_gemm_tiles": ([_P, ctypes.POINTER(c_int), ctypes.POINTER(c_int)], c_int),
     "pkt_runtime_set_timeout_ns": ([_P, ctypes.c_ulonglong], c_int),
     "pkt_runtime_set_task_accounting": ([_P, c_int], c_int),
+    "pkt_runtime_set_cta_pair": ([_P, c_int], c_int),
     "pkt_runtime_fetch_task_counter": ([_P, ctypes.POINTER(ctypes.c_ulonglong)], c_int),
     "pkt_runtime_set_perf": ([_P, c_int], c_int),
     "pkt_runtime_fetch_perf": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
@@ -99,6 +101,8 @@ _SIGS = {
     "pkt_mlp_set_grad_scale": ([_P, c_float], c_int),
     "pkt_mlp_forward_backward": ([_P, _P], c_int),
     "pkt_mlp_apply_update": ([_P, _P], c_int),
+    "pkt_mlp_set_perf": ([_P, c_int], c_int),
+    "pkt_mlp_fetch_perf": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
 }
 
 EXPORTS = sorted(_SIGS)

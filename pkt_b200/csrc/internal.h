@@ -67,7 +67,8 @@ constexpr int kLoadWarp = 1;
 constexpr int kMmaWarp = 2;
 constexpr int kEpiWarp0 = 3;
 constexpr int kEpiThreads = 128;
-constexpr int kStages = 4;
+constexpr int kStages = 4;       // single-CTA mode: 48 KB stages
+constexpr int kStagesPair = 6;   // pair mode: 32 KB stages (A 16 KB + half of B)
 constexpr int kSlots = 4;
 constexpr int kBM = 128;
 constexpr int kMaxBN = 256;
@@ -90,6 +91,8 @@ struct alignas(128) DevGemm {
   uint32_t a_lbo, b_lbo;   // descriptor leading-byte offsets
   uint32_t a_kstep, b_kstep;  // descriptor start advance per MMA (bytes)
   uint32_t a_box_bytes, b_box_bytes;
+  int pair;                     // 1: single CTA tiles (128 rows), 2: CTA-pair tiles (256 rows)
+  int b_rows;                   // rows of B (N direction) each CTA loads: bn / pair
   uint32_t a_sbo, b_sbo;        // descriptor stride-byte offsets
   uint32_t a_layout, b_layout;  // descriptor swizzle mode: 2 = 128B, 1 = 128B with 32B atoms
   int mma_per_kb;
@@ -109,6 +112,9 @@ enum PerfWord {
   kPerfEpiGemm = 8,
   kPerfEpiSimt = 9,
   kPerfTotal = 10,
+  kPerfMmaSlotWait = 11,   // MMA issuer waiting for the next task
+  kPerfMmaIssue = 12,      // MMA issuer between stage-full and commit
+  kPerfKBlocks = 13,       // k-blocks issued (count)
 };
 
 struct KParams {
@@ -127,8 +133,7 @@ struct KParams {
 constexpr int kStateHeader = 8;  // ints before the token counters
 inline int state_ints(int num_tokens) { return kStateHeader + 2 * num_tokens; }
 
-// Launches the megakernel (megakernel.cu).
-cudaError_t launch_megakernel(const KParams& p, int blocks, cudaStream_t stream);
-int megakernel_smem_bytes();
+// Launches the megakernel (megakernel.cu); pair = 2 launches clusters of two CTAs.
+cudaError_t launch_megakernel(const KParams& p, int blocks, cudaStream_t stream, int pair = 1);
 
 }  // namespace pkb

@@ -31,16 +31,22 @@ namespace pkb {
 
 namespace {
 
-struct Smem {
-  uint8_t stages[kStages][kStageBytes];  // 1024-byte aligned (kernel aligns the base)
+// P = 1: one CTA per tile, 4 stages of 48 KB (A 128x64 + B up to 256x64 bf16).
+// P = 2: CTA pairs, 6 stages of 32 KB (A 128x64 + this CTA's half of B).
+template <int P>
+struct SmemT {
+  static constexpr int NST = P == 2 ? kStagesPair : kStages;
+  static constexpr int SB = P == 2 ? kATileBytes + kBTileBytes / 2 : kStageBytes;
+  uint8_t stages[NST][SB];  // 1024-byte aligned (kernel aligns the base)
   pkt_task slots[kSlots];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[NST];
+  uint64_t empty[NST];
   uint64_t slot_full[kSlots];
   uint64_t slot_empty[kSlots];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t mma_drain;
+  uint64_t pair_done[kSlots];  // leader: the other CTA of the pair finished task seq
   uint32_t tmem_base;
   uint32_t pad0;
   float red[8][4][32];  // per 32-column chunk, per TMEM lane quadrant: column partial sums
@@ -49,7 +55,8 @@ struct Smem {
   double simt_redd[4];
 };
 
-constexpr int kSmemBytes = int(sizeof(Smem)) + 1024;
+template <int P>
+constexpr int smem_bytes() { return int(sizeof(SmemT<P>)) + 1024; }
 
 __device__ __forceinline__ int* tok_count(const KParams& p) { return p.state + kStateHeader; }
 __device__ __forceinline__ int* tok_epoch(const KParams& p) {
@@ -72,13 +79,20 @@ __device__ void set_error(const KParams& p, int code, int task, int detail) {
 // waiting for the controller's next task, which may itself be waiting on a
 // dependency with the same budget) get four budgets plus one second, so the
 // controller's dependency timeout is the one reported.
+template <bool CL = false>
+__device__ __forceinline__ bool try_wait_scoped(uint64_t* bar, uint32_t parity) {
+  return CL ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+}
+
+// CL: the barrier receives arrivals from the other CTA of a pair (cluster-scope acquire).
+template <bool CL = false>
 __device__ __forceinline__ bool wait_bar(const KParams& p, uint64_t* bar, uint32_t parity,
                                          int where, bool idle = false) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (try_wait_scoped<CL>(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   const uint64_t budget = idle ? 4 * p.timeout_ns + 1000000000ull : p.timeout_ns;
   uint32_t it = 0;
-  while (!mbar_try_wait(bar, parity)) {
+  while (!try_wait_scoped<CL>(bar, parity)) {
     if ((++it & 63u) == 0) {
       if (*status_word(p) != 0) return false;
       if (globaltimer_ns() - t0 > budget) {
@@ -104,8 +118,33 @@ __device__ __forceinline__ void copy_task(pkt_task* dst, const pkt_task* src) {
   for (int i = 0; i < 6; ++i) d[i] = s[i];
 }
 
+// Releases a slot of the ring: the ring lives in the leader CTA; the other CTA of a
+// pair arrives on the leader's slot_empty remotely.
+template <int P>
+__device__ __forceinline__ void release_slot(SmemT<P>& s, int slot, uint32_t rank) {
+  if (P == 1 || rank == 0)
+    mbar_arrive(&s.slot_empty[slot]);
+  else
+    mbar_arrive_remote(mapa_shared(smem_u32(&s.slot_empty[slot]), 0));
+}
+
+// Publishes a task into slot `slot` of this CTA and, for pairs, of the other CTA.
+template <int P>
+__device__ __forceinline__ void publish_slot(SmemT<P>& s, int slot, const pkt_task& task) {
+  copy_task(&s.slots[slot], &task);
+  if (P == 2) {
+    const uint32_t dst = mapa_shared(smem_u32(&s.slots[slot]), 1);
+    const int4* src = reinterpret_cast<const int4*>(&task);
+#pragma unroll
+    for (int i = 0; i < 6; ++i) st_cluster_v4(dst + 16 * i, src[i]);
+    mbar_arrive_remote(mapa_shared(smem_u32(&s.slot_full[slot]), 1));
+  }
+  mbar_arrive(&s.slot_full[slot]);
+}
+
 // ============================================================ controller
-__device__ void controller_loop(const KParams& p, Smem& s, unsigned long long* perf) {
+template <int P>
+__device__ void controller_loop(const KParams& p, SmemT<P>& s, unsigned long long* perf) {
   int seq = 0;
   unsigned long long dep_cycles = 0, slot_cycles = 0, ntasks = 0;
   int cursor_local = 0, cursor_end = 0;
@@ -134,7 +173,7 @@ __device__ void controller_loop(const KParams& p, Smem& s, unsigned long long* p
     if (h.opcode == PKT_OP_GEMM) {
       const pkt_gemm_tile_args* a = reinterpret_cast<const pkt_gemm_tile_args*>(task.args);
       if (int(a->gemm) >= p.num_gemms || int(a->tile_m) >= p.gemms[a->gemm].tiles_m ||
-          int(a->tile_n) >= p.gemms[a->gemm].tiles_n) {
+          int(a->tile_n) >= p.gemms[a->gemm].tiles_n || p.gemms[a->gemm].pair != P) {
         set_error(p, PKT_DEV_BAD_ARGS, t, -2);
         break;
       }
@@ -172,20 +211,20 @@ __device__ void controller_loop(const KParams& p, Smem& s, unsigned long long* p
     // ---- publish into the slot ring
     const int slot = seq % kSlots;
     const long long c1 = clock64();
-    if (!wait_bar(p, &s.slot_empty[slot], ((seq / kSlots) & 1) ^ 1, 1)) break;
+    if (!wait_bar<(P == 2)>(p, &s.slot_empty[slot], ((seq / kSlots) & 1) ^ 1, 1)) break;
     slot_cycles += clock64() - c1;
     task.header.user_tag = uint32_t(t);
-    copy_task(&s.slots[slot], &task);
     if (p.task_counter) atomicAdd(p.task_counter, 1ull);
-    mbar_arrive(&s.slot_full[slot]);
+    publish_slot<P>(s, slot, task);
     ++seq;
     ++ntasks;
   }
   // ---- stop marker: consumers leave their loops when they reach it
   const int slot = seq % kSlots;
-  if (wait_bar(p, &s.slot_empty[slot], ((seq / kSlots) & 1) ^ 1, 2)) {
-    s.slots[slot].header.opcode = kOpStop;
-    mbar_arrive(&s.slot_full[slot]);
+  if (wait_bar<(P == 2)>(p, &s.slot_empty[slot], ((seq / kSlots) & 1) ^ 1, 2)) {
+    pkt_task stop{};
+    stop.header.opcode = kOpStop;
+    publish_slot<P>(s, slot, stop);
   }
   if (perf) {
     perf[kPerfTasks] = ntasks;
@@ -195,16 +234,18 @@ __device__ void controller_loop(const KParams& p, Smem& s, unsigned long long* p
 }
 
 // ============================================================ loader (TMA producer)
-__device__ void loader_loop(const KParams& p, Smem& s, unsigned long long* perf) {
+template <int P>
+__device__ void loader_loop(const KParams& p, SmemT<P>& s, uint32_t rank, unsigned long long* perf) {
+  constexpr int NST = SmemT<P>::NST;
   int seq = 0;
   uint32_t stage = 0, phase = 0, issued = 0;
   unsigned long long wait_cycles = 0;
   while (true) {
     const int slot = seq % kSlots;
-    if (!wait_bar(p, &s.slot_full[slot], (seq / kSlots) & 1, 3, true)) break;
+    if (!wait_bar<(P == 2)>(p, &s.slot_full[slot], (seq / kSlots) & 1, 3, true)) break;
     const uint16_t op = s.slots[slot].header.opcode;
     pkt_gemm_tile_args ga = *reinterpret_cast<const pkt_gemm_tile_args*>(s.slots[slot].args);
-    mbar_arrive(&s.slot_empty[slot]);
+    release_slot<P>(s, slot, rank);
     ++seq;
     if (op == kOpStop) break;
     if (op != PKT_OP_GEMM) continue;
@@ -212,34 +253,52 @@ __device__ void loader_loop(const KParams& p, Smem& s, unsigned long long* perf)
     // Data of this tile was produced by other CTAs through generic stores and is
     // read here through the async proxy.
     fence_proxy_async_global();
-    const int m0 = int(ga.tile_m) * kBM;
-    const int n0 = int(ga.tile_n) * g.d.bn;
+    // pair mode: this CTA loads rows [rank*128, +128) of the 256-row A tile and
+    // rows [rank*bn/2, +bn/2) of B; both CTAs' bytes count on the leader's barrier
+    const int m0 = int(ga.tile_m) * kBM * P + int(rank) * kBM;
+    const int n0 = int(ga.tile_n) * g.d.bn + int(rank) * g.b_rows;
     bool ok = true;
     for (int kb = 0; kb < g.num_kb; ++kb) {
       const long long c0 = clock64();
-      if (!wait_bar(p, &s.empty[stage], phase ^ 1, 4)) {
+      if (!wait_bar<(P == 2)>(p, &s.empty[stage], phase ^ 1, 4)) {
         ok = false;
         break;
       }
       wait_cycles += clock64() - c0;
-      mbar_arrive_expect_tx(&s.full[stage], g.stage_tx);
+      if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], g.stage_tx);
       uint8_t* sa = s.stages[stage];
       uint8_t* sb = s.stages[stage] + kATileBytes;
       const int k0 = kb * g.bk;
-      if (g.d.a_major == PKT_MAJOR_K) {
-        tma_load_2d(sa, &g.map_a, &s.full[stage], k0, m0);
+      if (P == 1) {
+        if (g.d.a_major == PKT_MAJOR_K) {
+          tma_load_2d(sa, &g.map_a, &s.full[stage], k0, m0);
+        } else {
+          for (int i = 0; i < g.a_boxes; ++i)
+            tma_load_2d(sa + i * g.a_box_bytes, &g.map_a, &s.full[stage], m0 + i * g.box_mn, k0);
+        }
+        if (g.d.b_major == PKT_MAJOR_K) {
+          tma_load_2d(sb, &g.map_b, &s.full[stage], k0, n0);
+        } else {
+          for (int i = 0; i < g.b_boxes; ++i)
+            tma_load_2d(sb + i * g.b_box_bytes, &g.map_b, &s.full[stage], n0 + i * g.box_mn, k0);
+        }
       } else {
-        for (int i = 0; i < g.a_boxes; ++i)
-          tma_load_2d(sa + i * g.a_box_bytes, &g.map_a, &s.full[stage], m0 + i * g.box_mn, k0);
-      }
-      if (g.d.b_major == PKT_MAJOR_K) {
-        tma_load_2d(sb, &g.map_b, &s.full[stage], k0, n0);
-      } else {
-        for (int i = 0; i < g.b_boxes; ++i)
-          tma_load_2d(sb + i * g.b_box_bytes, &g.map_b, &s.full[stage], n0 + i * g.box_mn, k0);
+        const uint32_t fb = mapa_shared(smem_u32(&s.full[stage]), 0);  // leader's barrier
+        if (g.d.a_major == PKT_MAJOR_K) {
+          tma_load_2d_pair(sa, &g.map_a, fb, k0, m0);
+        } else {
+          for (int i = 0; i < g.a_boxes; ++i)
+            tma_load_2d_pair(sa + i * g.a_box_bytes, &g.map_a, fb, m0 + i * g.box_mn, k0);
+        }
+        if (g.d.b_major == PKT_MAJOR_K) {
+          tma_load_2d_pair(sb, &g.map_b, fb, k0, n0);
+        } else {
+          for (int i = 0; i < g.b_boxes; ++i)
+            tma_load_2d_pair(sb + i * g.b_box_bytes, &g.map_b, fb, n0 + i * g.box_mn, k0);
+        }
       }
       ++issued;
-      if (++stage == kStages) {
+      if (++stage == NST) {
         stage = 0;
         phase ^= 1;
       }
@@ -247,12 +306,14 @@ __device__ void loader_loop(const KParams& p, Smem& s, unsigned long long* perf)
     if (!ok) break;
   }
   // Drain: wait (bounded) until every issued stage landed, so no bulk copy can
-  // write into this CTA's shared memory after it exits.
-  const uint32_t n = issued < kStages ? issued : kStages;
+  // write into shared memory after the CTA exits. In pair mode the leader's
+  // barriers count both CTAs' bytes; the other CTA is held by the final cluster
+  // barrier until the leader has drained.
+  const uint32_t n = rank != 0 ? 0 : (issued < uint32_t(NST) ? issued : uint32_t(NST));
   for (uint32_t i = 0; i < n; ++i) {
-    const uint32_t idx = (stage + kStages - 1 - i) % kStages;
+    const uint32_t idx = (stage + NST - 1 - i) % NST;
     const uint32_t fill = issued - 1 - i;  // fill number of that stage
-    const uint32_t par = (fill / kStages) & 1;
+    const uint32_t par = (fill / NST) & 1;
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(&s.full[idx], par)) {
       if (globaltimer_ns() - t0 > p.timeout_ns) break;
@@ -262,25 +323,29 @@ __device__ void loader_loop(const KParams& p, Smem& s, unsigned long long* perf)
 }
 
 // ============================================================ MMA issuer
-__device__ void mma_loop(const KParams& p, Smem& s, uint32_t tmem_base,
+template <int P>
+__device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
                          unsigned long long* perf) {
+  constexpr int NST = SmemT<P>::NST;
   int seq = 0;
   uint32_t stage = 0, phase = 0, gemm_count = 0;
-  unsigned long long full_wait = 0, tmem_wait = 0, tiles = 0;
+  unsigned long long full_wait = 0, tmem_wait = 0, tiles = 0, slot_wait = 0, issue = 0, kblocks = 0;
   bool any_mma = false;
   while (true) {
     const int slot = seq % kSlots;
-    if (!wait_bar(p, &s.slot_full[slot], (seq / kSlots) & 1, 5, true)) break;
+    const long long cs = clock64();
+    if (!wait_bar<(P == 2)>(p, &s.slot_full[slot], (seq / kSlots) & 1, 5, true)) break;
+    slot_wait += clock64() - cs;
     const uint16_t op = s.slots[slot].header.opcode;
     pkt_gemm_tile_args ga = *reinterpret_cast<const pkt_gemm_tile_args*>(s.slots[slot].args);
-    mbar_arrive(&s.slot_empty[slot]);
+    mbar_arrive(&s.slot_empty[slot]);  // the MMA issuer only runs in the leader CTA
     ++seq;
     if (op == kOpStop) break;
     if (op != PKT_OP_GEMM) continue;
     const DevGemm& g = p.gemms[ga.gemm];
     const uint32_t acc = gemm_count & 1, use = gemm_count >> 1;
     const long long c0 = clock64();
-    if (!wait_bar(p, &s.tmem_empty[acc], (use & 1) ^ 1, 6)) break;
+    if (!wait_bar<(P == 2)>(p, &s.tmem_empty[acc], (use & 1) ^ 1, 6)) break;
     tmem_wait += clock64() - c0;
     tc_fence_after();
     const uint32_t d_tmem = tmem_base + acc * 256;
@@ -288,11 +353,12 @@ __device__ void mma_loop(const KParams& p, Smem& s, uint32_t tmem_base,
     bool ok = true;
     for (int kb = 0; kb < g.num_kb; ++kb) {
       const long long c1 = clock64();
-      if (!wait_bar(p, &s.full[stage], phase, 7)) {
+      if (!wait_bar<(P == 2)>(p, &s.full[stage], phase, 7)) {
         ok = false;
         break;
       }
-      full_wait += clock64() - c1;
+      const long long c2 = clock64();
+      full_wait += c2 - c1;
       tc_fence_after();
       const uint32_t sa = smem_u32(s.stages[stage]);
       const uint32_t sb = sa + kATileBytes;
@@ -301,26 +367,45 @@ __device__ void mma_loop(const KParams& p, Smem& s, uint32_t tmem_base,
         const uint64_t ad = smem_desc(sa + k * g.a_kstep, g.a_lbo, g.a_sbo, g.a_layout);
         const uint64_t bd = smem_desc(sb + k * g.b_kstep, g.b_lbo, g.b_sbo, g.b_layout);
         const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-        if (tf32)
-          mma_tf32(d_tmem, ad, bd, g.idesc, accum);
-        else
-          mma_bf16(d_tmem, ad, bd, g.idesc, accum);
+        if (P == 2) {
+          if (tf32)
+            mma_tf32_pair(d_tmem, ad, bd, g.idesc, accum);
+          else
+            mma_bf16_pair(d_tmem, ad, bd, g.idesc, accum);
+        } else {
+          if (tf32)
+            mma_tf32(d_tmem, ad, bd, g.idesc, accum);
+          else
+            mma_bf16(d_tmem, ad, bd, g.idesc, accum);
+        }
       }
       any_mma = true;
-      mma_commit(&s.empty[stage]);  // stage reusable once these MMAs have read it
-      if (++stage == kStages) {
+      // stage reusable (in both CTAs of a pair) once these MMAs have read it
+      if (P == 2)
+        mma_commit_pair_both(&s.empty[stage]);
+      else
+        mma_commit(&s.empty[stage]);
+      issue += clock64() - c2;
+      ++kblocks;
+      if (++stage == NST) {
         stage = 0;
         phase ^= 1;
       }
     }
     if (!ok) break;
-    mma_commit(&s.tmem_full[acc]);  // accumulator complete
+    if (P == 2)
+      mma_commit_pair_both(&s.tmem_full[acc]);  // accumulator complete in both CTAs
+    else
+      mma_commit(&s.tmem_full[acc]);
     ++gemm_count;
     ++tiles;
   }
   if (any_mma) {
     // Every MMA this thread issued has finished before TMEM is released.
-    mma_commit(&s.mma_drain);
+    if (P == 2)
+      mma_commit_pair_local(&s.mma_drain);
+    else
+      mma_commit(&s.mma_drain);
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(&s.mma_drain, 0)) {
       if (globaltimer_ns() - t0 > p.timeout_ns) break;
@@ -330,14 +415,20 @@ __device__ void mma_loop(const KParams& p, Smem& s, uint32_t tmem_base,
     perf[kPerfGemmTiles] = tiles;
     perf[kPerfMmaFullWait] = full_wait;
     perf[kPerfMmaTmemWait] = tmem_wait;
+    perf[kPerfMmaSlotWait] = slot_wait;
+    perf[kPerfMmaIssue] = issue;
+    perf[kPerfKBlocks] = kblocks;
   }
 }
 
 // ============================================================ epilogue helpers
 struct EpiCtx {
-  int et;    // 0..127 thread index among the compute warps
+  int et;    // 0..127 thread index among the compute warps of this CTA
   int lane;
   int q;     // TMEM lane quadrant of this warp (warp id % 4)
+  uint32_t rank;  // CTA rank in its pair (0 when single)
+  int tid;   // thread index across the pair's compute warps
+  int nthr;  // compute threads across the pair (128 or 256)
 };
 
 __device__ __forceinline__ void epi_sync() { named_barrier_sync(1, kEpiThreads); }
@@ -443,17 +534,19 @@ __device__ __forceinline__ bool aligned16(const void* p) {
 }
 
 // ============================================================ GEMM epilogue
-__device__ void epilogue_gemm(const KParams& p, Smem& s, const EpiCtx& c, const DevGemm& g,
+template <int P>
+__device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, const DevGemm& g,
                               int tile_m, int tile_n, uint32_t tmem_base, uint32_t acc,
                               uint32_t use, unsigned long long& tmem_wait) {
   const pkt_gemm_desc& d = g.d;
   const long long c0 = clock64();
-  wait_bar(p, &s.tmem_full[acc], use & 1, 8);
+  wait_bar<(P == 2)>(p, &s.tmem_full[acc], use & 1, 8);
   tmem_wait += clock64() - c0;
   __syncwarp();  // tcgen05.ld is warp-collective
   tc_fence_after();
 
-  const int row = tile_m * kBM + c.q * 32 + c.lane;
+  const int rblock = tile_m * P + int(c.rank);  // 128-row block of this CTA's rows
+  const int row = rblock * kBM + c.q * 32 + c.lane;
   const bool row_ok = row < d.M;
   const int n0 = tile_n * d.bn;
   const int nchunks = (d.bn + 31) / 32;
@@ -573,7 +666,12 @@ __device__ void epilogue_gemm(const KParams& p, Smem& s, const EpiCtx& c, const 
   // Accumulator fully read: hand it back to the MMA warp.
   tc_fence_before();
   __syncwarp();
-  if (c.lane == 0) mbar_arrive(&s.tmem_empty[acc]);
+  if (c.lane == 0) {
+    if (P == 1 || c.rank == 0)
+      mbar_arrive(&s.tmem_empty[acc]);
+    else
+      mbar_arrive_remote(mapa_shared(smem_u32(&s.tmem_empty[acc]), 0));
+  }
 
   if (epi == PKT_EPI_MSE && d.loss_partials != nullptr) {
 #pragma unroll
@@ -588,31 +686,33 @@ __device__ void epilogue_gemm(const KParams& p, Smem& s, const EpiCtx& c, const 
         const int col = n0 + ch * 32 + j;
         if (col < d.N && ch * 32 + j < d.bn) {
           const float tot = ((s.red[ch][0][j] + s.red[ch][1][j]) + s.red[ch][2][j]) + s.red[ch][3][j];
-          d.colsum[(long long)tile_m * d.ldcol + col] = tot;
+          d.colsum[(long long)rblock * d.ldcol + col] = tot;
         }
       }
     }
     if (epi == PKT_EPI_MSE && d.loss_partials != nullptr && c.et == 0) {
-      d.loss_partials[tile_m * g.tiles_n + tile_n] =
+      d.loss_partials[rblock * g.tiles_n + tile_n] =
           ((s.lossred[0] + s.lossred[1]) + s.lossred[2]) + s.lossred[3];
     }
   }
 }
 
-// ============================================================ SIMT ops (128 threads)
-__device__ void op_axpy(const AxpyArgs& a, int et) {
+// ============================================================ SIMT ops
+// Element-wise ops stride over every compute thread of the CTA (or CTA pair):
+// `et` is the thread's index, `nthr` the thread count.
+__device__ void op_axpy(const AxpyArgs& a, int et, int nthr) {
   const long long n = a.n;
   if (aligned16(a.x) && aligned16(a.y)) {
     const long long n4 = n >> 2;
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
     float4* y4 = reinterpret_cast<float4*>(a.y);
     long long i = et;
-    for (; i + 3 * kEpiThreads < n4; i += 4 * kEpiThreads) {
+    for (; i + 3 * nthr < n4; i += 4 * nthr) {
       float4 xv[4], yv[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        xv[u] = x4[i + u * kEpiThreads];
-        yv[u] = y4[i + u * kEpiThreads];
+        xv[u] = x4[i + u * nthr];
+        yv[u] = y4[i + u * nthr];
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -620,10 +720,10 @@ __device__ void op_axpy(const AxpyArgs& a, int et) {
         yv[u].y = fmaf(a.a, xv[u].y, yv[u].y);
         yv[u].z = fmaf(a.a, xv[u].z, yv[u].z);
         yv[u].w = fmaf(a.a, xv[u].w, yv[u].w);
-        y4[i + u * kEpiThreads] = yv[u];
+        y4[i + u * nthr] = yv[u];
       }
     }
-    for (; i < n4; i += kEpiThreads) {
+    for (; i < n4; i += nthr) {
       const float4 xv = x4[i];
       float4 yv = y4[i];
       yv.x = fmaf(a.a, xv.x, yv.x);
@@ -632,28 +732,28 @@ __device__ void op_axpy(const AxpyArgs& a, int et) {
       yv.w = fmaf(a.a, xv.w, yv.w);
       y4[i] = yv;
     }
-    for (long long k = n4 * 4 + et; k < n; k += kEpiThreads) a.y[k] = fmaf(a.a, a.x[k], a.y[k]);
+    for (long long k = n4 * 4 + et; k < n; k += nthr) a.y[k] = fmaf(a.a, a.x[k], a.y[k]);
   } else {
-    for (long long k = et; k < n; k += kEpiThreads) a.y[k] = fmaf(a.a, a.x[k], a.y[k]);
+    for (long long k = et; k < n; k += nthr) a.y[k] = fmaf(a.a, a.x[k], a.y[k]);
   }
 }
 
-__device__ void op_zero(const ZeroMemoryArgs& a, int et) {
+__device__ void op_zero(const ZeroMemoryArgs& a, int et, int nthr) {
   const long long n = a.size;
   if (aligned16(a.ptr)) {
     const long long n4 = n >> 2;
     float4* p4 = reinterpret_cast<float4*>(a.ptr);
-    for (long long i = et; i < n4; i += kEpiThreads) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (long long k = n4 * 4 + et; k < n; k += kEpiThreads) a.ptr[k] = 0.f;
+    for (long long i = et; i < n4; i += nthr) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (long long k = n4 * 4 + et; k < n; k += nthr) a.ptr[k] = 0.f;
   } else {
-    for (long long k = et; k < n; k += kEpiThreads) a.ptr[k] = 0.f;
+    for (long long k = et; k < n; k += nthr) a.ptr[k] = 0.f;
   }
 }
 
 // w_out = w - lr*g (single-rounding fma, as nvcc compiles pkt's `W[i] -= lr*dW[i]`,
 // include/ops/sgd.cuh:41-43), optionally also writing the bf16 copy of w_out.
 __device__ void op_sgd(const float* W, const float* dW, float* Wo, float lr, long long n,
-                       uint16_t* shadow, int et) {
+                       uint16_t* shadow, int et, int nthr) {
   const bool vec = aligned16(W) && aligned16(dW) && aligned16(Wo) &&
                    (shadow == nullptr || (reinterpret_cast<uintptr_t>(shadow) & 7u) == 0);
   long long head = 0;
@@ -663,12 +763,12 @@ __device__ void op_sgd(const float* W, const float* dW, float* Wo, float lr, lon
     const float4* g4 = reinterpret_cast<const float4*>(dW);
     float4* o4 = reinterpret_cast<float4*>(Wo);
     long long i = et;
-    for (; i + 3 * kEpiThreads < n4; i += 4 * kEpiThreads) {
+    for (; i + 3 * nthr < n4; i += 4 * nthr) {
       float4 w[4], g[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        w[u] = w4[i + u * kEpiThreads];
-        g[u] = g4[i + u * kEpiThreads];
+        w[u] = w4[i + u * nthr];
+        g[u] = g4[i + u * nthr];
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -676,13 +776,13 @@ __device__ void op_sgd(const float* W, const float* dW, float* Wo, float lr, lon
         w[u].y = fmaf(-lr, g[u].y, w[u].y);
         w[u].z = fmaf(-lr, g[u].z, w[u].z);
         w[u].w = fmaf(-lr, g[u].w, w[u].w);
-        o4[i + u * kEpiThreads] = w[u];
+        o4[i + u * nthr] = w[u];
         if (shadow)
-          reinterpret_cast<uint2*>(shadow)[i + u * kEpiThreads] =
+          reinterpret_cast<uint2*>(shadow)[i + u * nthr] =
               make_uint2(pack_bf16x2(w[u].x, w[u].y), pack_bf16x2(w[u].z, w[u].w));
       }
     }
-    for (; i < n4; i += kEpiThreads) {
+    for (; i < n4; i += nthr) {
       float4 w = w4[i];
       const float4 g = g4[i];
       w.x = fmaf(-lr, g.x, w.x);
@@ -695,7 +795,7 @@ __device__ void op_sgd(const float* W, const float* dW, float* Wo, float lr, lon
     }
     head = n4 * 4;
   }
-  for (long long k = head + et; k < n; k += kEpiThreads) {
+  for (long long k = head + et; k < n; k += nthr) {
     const float w = fmaf(-lr, dW[k], W[k]);
     Wo[k] = w;
     if (shadow) shadow[k] = f32_to_bf16_rn(w);
@@ -703,7 +803,8 @@ __device__ void op_sgd(const float* W, const float* dW, float* Wo, float lr, lon
 }
 
 // Deterministic sum over the 128 compute threads (fixed order), result on et == 0.
-__device__ float epi_block_sum(Smem& s, const EpiCtx& c, float v) {
+template <int P>
+__device__ float epi_block_sum(SmemT<P>& s, const EpiCtx& c, float v) {
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
   if (c.lane == 0) s.simt_red[c.et >> 5] = v;
@@ -713,7 +814,8 @@ __device__ float epi_block_sum(Smem& s, const EpiCtx& c, float v) {
   return tot;
 }
 
-__device__ void op_mse(Smem& s, const EpiCtx& c, const MSELossArgs& a) {
+template <int P>
+__device__ void op_mse(SmemT<P>& s, const EpiCtx& c, const MSELossArgs& a) {
   const long long elems = (long long)a.batch * a.m;
   const float scale = 2.0f / float(a.batch * a.m);
   float part = 0.f;
@@ -726,12 +828,12 @@ __device__ void op_mse(Smem& s, const EpiCtx& c, const MSELossArgs& a) {
   if (c.et == 0) atomicAdd(a.loss, tot / float(elems));
 }
 
-__device__ void op_linear_forward(const LinearForwardArgs& a, int et) {
+__device__ void op_linear_forward(const LinearForwardArgs& a, int et, int nthr) {
   // y[b, j] = sum_k x[b, k] W[j, k] over the task's tile (include/ops/linear_fwd.cuh:18-29),
   // fp32 throughout (pkt rounds x to fp16 first; this path keeps full fp32).
   const int rows = a.tile_m_count, cols = a.tile_n_count;
   const long long total = (long long)rows * cols;
-  for (long long o = et; o < total; o += kEpiThreads) {
+  for (long long o = et; o < total; o += nthr) {
     const int b = a.tile_m_start + int(o / cols);
     const int j = a.tile_n_start + int(o % cols);
     if (b >= a.batch || j >= a.m) continue;
@@ -743,11 +845,11 @@ __device__ void op_linear_forward(const LinearForwardArgs& a, int et) {
   }
 }
 
-__device__ void op_linear_backward(const LinearBackwardArgs& a, int et) {
+__device__ void op_linear_backward(const LinearBackwardArgs& a, int et, int nthr) {
   // dW[r, c] = sum_b dy[b, r] x[b, c], overwriting the tile (include/ops/linear_bwd.cuh:94-157).
   const int rows = a.tile_m_count, cols = a.tile_n_count;
   const long long total = (long long)rows * cols;
-  for (long long o = et; o < total; o += kEpiThreads) {
+  for (long long o = et; o < total; o += nthr) {
     const int r = a.tile_m_start + int(o / cols);
     const int cc = a.tile_n_start + int(o % cols);
     if (r >= a.m || cc >= a.n) continue;
@@ -757,8 +859,8 @@ __device__ void op_linear_backward(const LinearBackwardArgs& a, int et) {
   }
 }
 
-__device__ void op_bias_sgd(const pkt_bias_sgd_args& a, int et) {
-  for (int col = a.col_begin + et; col < a.col_end; col += kEpiThreads) {
+__device__ void op_bias_sgd(const pkt_bias_sgd_args& a, int et, int nthr) {
+  for (int col = a.col_begin + et; col < a.col_end; col += nthr) {
     float sum = 0.f;
     for (int pidx = 0; pidx < a.num_partials; ++pidx) sum += a.partials[(long long)pidx * a.ld + col];
     if (a.grad_out) a.grad_out[col] = sum;
@@ -766,7 +868,8 @@ __device__ void op_bias_sgd(const pkt_bias_sgd_args& a, int et) {
   }
 }
 
-__device__ void op_loss_reduce(Smem& s, const EpiCtx& c, const pkt_loss_reduce_args& a) {
+template <int P>
+__device__ void op_loss_reduce(SmemT<P>& s, const EpiCtx& c, const pkt_loss_reduce_args& a) {
   double part = 0.0;
   for (int i = c.et; i < a.count; i += kEpiThreads) part += double(a.partials[i]);
 #pragma unroll
@@ -783,18 +886,19 @@ __device__ void op_loss_reduce(Smem& s, const EpiCtx& c, const pkt_loss_reduce_a
 }
 
 // ============================================================ compute warps
-__device__ void compute_loop(const KParams& p, Smem& s, uint32_t tmem_base, const EpiCtx& c,
+template <int P>
+__device__ void compute_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base, const EpiCtx& c,
                              unsigned long long* perf) {
   int seq = 0;
   uint32_t gemm_count = 0;
   unsigned long long tmem_wait = 0, gemm_cycles = 0, simt_cycles = 0;
   while (true) {
     const int slot = seq % kSlots;
-    if (!wait_bar(p, &s.slot_full[slot], (seq / kSlots) & 1, 9, true)) break;
+    if (!wait_bar<(P == 2)>(p, &s.slot_full[slot], (seq / kSlots) & 1, 9, true)) break;
     pkt_task task;
     copy_task(&task, &s.slots[slot]);
     epi_sync();  // every compute thread has its copy
-    if (c.et == 0) mbar_arrive(&s.slot_empty[slot]);
+    if (c.et == 0) release_slot<P>(s, slot, c.rank);
     ++seq;
     const uint16_t op = task.header.opcode;
     if (op == kOpStop) break;
@@ -803,41 +907,42 @@ __device__ void compute_loop(const KParams& p, Smem& s, uint32_t tmem_base, cons
       case PKT_OP_GEMM: {
         const pkt_gemm_tile_args& ga = *reinterpret_cast<const pkt_gemm_tile_args*>(task.args);
         const uint32_t acc = gemm_count & 1, use = gemm_count >> 1;
-        epilogue_gemm(p, s, c, p.gemms[ga.gemm], int(ga.tile_m), int(ga.tile_n), tmem_base, acc,
-                      use, tmem_wait);
+        epilogue_gemm<P>(p, s, c, p.gemms[ga.gemm], int(ga.tile_m), int(ga.tile_n), tmem_base, acc,
+                         use, tmem_wait);
         ++gemm_count;
         break;
       }
       case PKT_OP_AXPY:
-        op_axpy(*reinterpret_cast<const AxpyArgs*>(task.args), c.et);
+        op_axpy(*reinterpret_cast<const AxpyArgs*>(task.args), c.tid, c.nthr);
         break;
       case PKT_OP_ZERO_MEMORY:
-        op_zero(*reinterpret_cast<const ZeroMemoryArgs*>(task.args), c.et);
+        op_zero(*reinterpret_cast<const ZeroMemoryArgs*>(task.args), c.tid, c.nthr);
         break;
       case PKT_OP_SGD_UPDATE: {
         const SGDUpdateArgs& a = *reinterpret_cast<const SGDUpdateArgs*>(task.args);
-        op_sgd(a.W, a.dW, a.W, a.lr, a.size, nullptr, c.et);
+        op_sgd(a.W, a.dW, a.W, a.lr, a.size, nullptr, c.tid, c.nthr);
         break;
       }
       case PKT_OP_SGD_MIXED: {
         const pkt_sgd_mixed_args& a = *reinterpret_cast<const pkt_sgd_mixed_args*>(task.args);
-        op_sgd(a.w, a.g, a.w_out ? a.w_out : const_cast<float*>(a.w), a.lr, a.n, a.w_bf16, c.et);
+        op_sgd(a.w, a.g, a.w_out ? a.w_out : const_cast<float*>(a.w), a.lr, a.n, a.w_bf16, c.tid,
+               c.nthr);
         break;
       }
       case PKT_OP_MSE_LOSS:
-        op_mse(s, c, *reinterpret_cast<const MSELossArgs*>(task.args));
+        if (c.rank == 0) op_mse<P>(s, c, *reinterpret_cast<const MSELossArgs*>(task.args));
         break;
       case PKT_OP_LINEAR_FORWARD:
-        op_linear_forward(*reinterpret_cast<const LinearForwardArgs*>(task.args), c.et);
+        op_linear_forward(*reinterpret_cast<const LinearForwardArgs*>(task.args), c.tid, c.nthr);
         break;
       case PKT_OP_LINEAR_BACKWARD:
-        op_linear_backward(*reinterpret_cast<const LinearBackwardArgs*>(task.args), c.et);
+        op_linear_backward(*reinterpret_cast<const LinearBackwardArgs*>(task.args), c.tid, c.nthr);
         break;
       case PKT_OP_BIAS_SGD:
-        op_bias_sgd(*reinterpret_cast<const pkt_bias_sgd_args*>(task.args), c.et);
+        op_bias_sgd(*reinterpret_cast<const pkt_bias_sgd_args*>(task.args), c.tid, c.nthr);
         break;
       case PKT_OP_LOSS_REDUCE:
-        op_loss_reduce(s, c, *reinterpret_cast<const pkt_loss_reduce_args*>(task.args));
+        if (c.rank == 0) op_loss_reduce<P>(s, c, *reinterpret_cast<const pkt_loss_reduce_args*>(task.args));
         break;
       default:  // PKT_OP_INVALID: no work, tokens are still published
         break;
@@ -851,7 +956,16 @@ __device__ void compute_loop(const KParams& p, Smem& s, uint32_t tmem_base, cons
     __threadfence();
     fence_proxy_async_global();
     epi_sync();
-    if (c.et == 0) {
+    if (P == 2 && c.et == 0) {
+      // pair: the leader publishes once the other CTA's half is stored too
+      const int ps = (seq - 1) % kSlots;
+      if (c.rank != 0) {
+        mbar_arrive_remote(mapa_shared(smem_u32(&s.pair_done[ps]), 0));
+      } else {
+        wait_bar<true>(p, &s.pair_done[ps], ((seq - 1) / kSlots) & 1, 10);
+      }
+    }
+    if (c.et == 0 && c.rank == 0) {
       const pkt_task_header& h = task.header;
       if (h.buffer_write_id != 0) {
         atomicMax(tok_epoch(p) + h.buffer_write_id, int(h.write_epoch));
@@ -868,80 +982,115 @@ __device__ void compute_loop(const KParams& p, Smem& s, uint32_t tmem_base, cons
   }
 }
 
+// P = 1: every CTA works alone. P = 2: launched in clusters of two; the pair
+// shares one task ring (rank 0's controller feeds both CTAs), rank 0 issues the
+// cta_group::2 MMAs for 256-row tiles, both CTAs load their operand halves and
+// run the epilogue for their 128 rows.
+template <int P>
 __global__ void __launch_bounds__(kThreads, 1) pk_megakernel(const __grid_constant__ KParams p) {
   extern __shared__ uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                     ~uintptr_t(1023));
+  SmemT<P>& s = *reinterpret_cast<SmemT<P>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  constexpr int NST = SmemT<P>::NST;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = P == 2 ? cluster_ctarank() : 0;
   unsigned long long* perf = p.perf ? p.perf + (size_t)blockIdx.x * PKT_PERF_WORDS : nullptr;
   const long long t_start = clock64();
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < NST; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&s.slot_full[i], 1);
-      mbar_init(&s.slot_empty[i], 3);  // loader, MMA issuer, compute warps
+      // leader: loader, MMA issuer, compute warps (+ the other CTA's loader and compute warps)
+      mbar_init(&s.slot_empty[i], P == 2 ? 5 : 3);
+      mbar_init(&s.pair_done[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.tmem_full[i], 1);
-      mbar_init(&s.tmem_empty[i], 4);  // one arrive per compute warp
+      mbar_init(&s.tmem_empty[i], 4 * P);  // one arrive per compute warp (of both CTAs)
     }
     mbar_init(&s.mma_drain, 1);
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(&s.tmem_base, kTmemCols);
-    tmem_relinquish();
+    if (P == 2) {
+      tmem_alloc_pair(&s.tmem_base, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&s.tmem_base, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (P == 2) cluster_sync();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = s.tmem_base;
 
   if (warp == kCtrlWarp) {
-    if (lane == 0) controller_loop(p, s, perf);
+    if (lane == 0 && rank == 0) controller_loop<P>(p, s, perf);
     __syncwarp();
   } else if (warp == kLoadWarp) {
-    if (lane == 0) loader_loop(p, s, perf);
+    if (lane == 0) loader_loop<P>(p, s, rank, perf);
     __syncwarp();
   } else if (warp == kMmaWarp) {
-    if (lane == 0) mma_loop(p, s, tmem_base, perf);
+    if (lane == 0 && rank == 0) mma_loop<P>(p, s, tmem_base, perf);
     __syncwarp();
   } else {
-    EpiCtx c{int(threadIdx.x) - kEpiWarp0 * 32, lane, warp & 3};
-    compute_loop(p, s, tmem_base, c, perf);
+    const int et = int(threadIdx.x) - kEpiWarp0 * 32;
+    EpiCtx c{et, lane, warp & 3, rank, int(rank) * kEpiThreads + et, kEpiThreads * P};
+    compute_loop<P>(p, s, tmem_base, c, perf);
   }
 
   tc_fence_before();
   __syncthreads();
+  if (P == 2) cluster_sync();  // neither CTA releases TMEM / exits while the other still works
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if (P == 2)
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    else
+      tmem_dealloc(tmem_base, kTmemCols);
   }
   if (perf && threadIdx.x == 0) perf[kPerfTotal] = clock64() - t_start;
 }
 
-}  // namespace
-
-int megakernel_smem_bytes() { return kSmemBytes; }
-
-cudaError_t launch_megakernel(const KParams& p, int blocks, cudaStream_t stream) {
+template <int P>
+cudaError_t launch_variant(const KParams& p, int blocks, cudaStream_t stream) {
   // The attribute is per device; set it on every device this process launches on.
   static unsigned long long attr_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !(attr_mask & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(pk_megakernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(pk_megakernel<P>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<P>());
     if (e != cudaSuccess) return e;
     attr_mask |= 1ull << dev;
   }
-  pk_megakernel<<<blocks, kThreads, kSmemBytes, stream>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem_bytes<P>();
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = P;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, pk_megakernel<P>, p);
+}
+
+}  // namespace
+
+cudaError_t launch_megakernel(const KParams& p, int blocks, cudaStream_t stream, int pair) {
+  if (pair == 2) return launch_variant<2>(p, blocks, stream);
+  return launch_variant<1>(p, blocks, stream);
 }
 
 }  // namespace pkb

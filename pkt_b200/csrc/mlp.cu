@@ -83,7 +83,9 @@ struct Mlp {
   std::vector<long long> dW_off, db_off;
 
   int parity = 0;
-  int TM = 0;
+  int P = 2;    // CTA pair (cta_group::2, 256-row tiles) or single CTA (128-row tiles)
+  int TM = 0;   // row tiles of the batch-row GEMMs: ceil(B / (128 P))
+  int TMr = 0;  // 128-row blocks of the batch (TM * P): rows of the column / loss partials
   // step task lists by [weight parity][input slot]; update lists by weight parity
   std::vector<pkt_task> tasks[2][2], update[2];
   pkt_task* d_tasks[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
@@ -126,14 +128,16 @@ struct Mlp {
   float* Wmaster(int l, int p) const { return bf ? W32[0][l] : W32[p][l]; }
 
   int pick_bn(int M, int N, bool b_mn) const {
-    const int align = b_mn ? (bf ? 64 : 32) : 16;
+    // each CTA of a pair holds bn/P rows of B: a multiple of the 128-byte MN atom
+    // (MN-major) or of 16 (K-major)
+    const int align = (b_mn ? (bf ? 64 : 32) : 16) * P;
     int cap = std::min(max_bn, kMaxBN);
     int need = round_up(N, align);
     int bn = std::min(cap, need);
     bn = std::max(align, bn / align * align);
-    const int tiles_m = (M + kBM - 1) / kBM;
+    const int tiles_m = (M + kBM * P - 1) / (kBM * P);
     // shrink the tile until the GEMM alone fills the SMs (small layers)
-    while (bn > std::max(64, align) && (long long)tiles_m * ((N + bn - 1) / bn) < rt->num_sms) {
+    while (bn > std::max(64 * P, align) && (long long)tiles_m * ((N + bn - 1) / bn) < rt->num_sms) {
       const int nb = bn / 2;
       if (nb % align != 0) break;
       bn = nb;
@@ -171,7 +175,9 @@ int Mlp::setup(const pkt_mlp_config& c) {
   if (grad_mode != 0 && grad_mode != 1) return fail(PKT_ERR_ARGS, "grad_mode must be 0 or 1");
   ld.resize(L + 1);
   for (int l = 0; l <= L; ++l) ld[l] = round_up(dims[l], 64);
-  TM = (B + kBM - 1) / kBM;
+  P = c.cta_pair == 1 ? 1 : 2;
+  TM = (B + kBM * P - 1) / (kBM * P);
+  TMr = TM * P;
   int rc;
   for (int k = 0; k < 2; ++k) {
     if ((rc = alloc(&Xs[k], size_t(B) * ld[0] * es))) return rc;
@@ -200,9 +206,9 @@ int Mlp::setup(const pkt_mlp_config& c) {
   colsum.assign(L, nullptr);
   for (int l = 0; l < L; ++l) {
     if ((rc = alloc((void**)&bias[l], size_t(ld[l + 1]) * 4))) return rc;
-    if (has_bias && (rc = alloc((void**)&colsum[l], size_t(TM) * ld[l + 1] * 4))) return rc;
+    if (has_bias && (rc = alloc((void**)&colsum[l], size_t(TMr) * ld[l + 1] * 4))) return rc;
   }
-  if ((rc = alloc((void**)&loss_partials, size_t(TM) * 64 * 4 + size_t(TM) * ((dims[L] + 15) / 16) * 4))) return rc;
+  if ((rc = alloc((void**)&loss_partials, size_t(TMr) * 64 * 4 + size_t(TMr) * ((dims[L] + 15) / 16) * 4))) return rc;
   if ((rc = alloc((void**)&losses, size_t(loss_cap) * 4))) return rc;
   if ((rc = alloc((void**)&step_ctr, 16))) return rc;
   if ((rc = alloc((void**)&Yout, size_t(B) * ld[L] * 4))) return rc;
@@ -267,6 +273,7 @@ int Mlp::build(int p, int q) {
       d.ldy = ld[L];
     }
     fwd[l] = int(g.size());
+    d.cta_pair = P;
     g.push_back(d);
   }
   // ---- dgrad (l >= 1) and wgrad
@@ -293,7 +300,8 @@ int Mlp::build(int p, int q) {
       d.colsum = has_bias ? colsum[l - 1] : nullptr;
       d.ldcol = ld[l];
       dgr[l] = int(g.size());
-      g.push_back(d);
+      d.cta_pair = P;
+    g.push_back(d);
     }
     pkt_gemm_desc d{};
     d.M = dims[l + 1];
@@ -322,6 +330,7 @@ int Mlp::build(int p, int q) {
       d.out_dtype = PKT_DTYPE_F32;
     }
     wgr[l] = int(g.size());
+    d.cta_pair = P;
     g.push_back(d);
   }
   int first = 0;
@@ -377,7 +386,7 @@ int Mlp::build(int p, int q) {
     const DevGemm& dg = G(fwd[L - 1]);
     pkt_task t{};
     t.header.opcode = PKT_OP_LOSS_REDUCE;
-    pkt_loss_reduce_args a{loss_partials, losses, dg.tiles_m * dg.tiles_n,
+    pkt_loss_reduce_args a{loss_partials, losses, dg.tiles_m * P * dg.tiles_n,
                            float(1.0 / (double(B) * double(dims[L]))), step_ctr};
     t.header.arg_bytes = sizeof(a);
     std::memcpy(t.args, &a, sizeof(a));
@@ -385,20 +394,24 @@ int Mlp::build(int p, int q) {
     t.header.wait_count = uint32_t(TM * dg.tiles_n);
     tl.push_back(t);
   }
+  // The dgrad chain (the critical path) first, row block by row block; the
+  // weight-gradient tiles, which only need a complete dY_l, after it: by the time
+  // a CTA dequeues them their inputs are normally complete, so the controller
+  // rarely blocks on a token.
+  for (int l = L - 1; l >= 1; --l) {
+    const DevGemm& dg = G(dgr[l]);
+    for (int i = 0; i < TM; ++i)
+      for (int j = 0; j < dg.tiles_n; ++j) {
+        pkt_task t = gemm_task(dgr[l], i, j);
+        t.header.buffer_read_id = uint16_t(Bk[l][i]);
+        t.header.wait_count = uint32_t(dy_tn[l]);
+        t.header.buffer_write_id = uint16_t(Bk[l - 1][i]);
+        t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
+        tl.push_back(t);
+        ++tiles;
+      }
+  }
   for (int l = L - 1; l >= 0; --l) {
-    if (l >= 1) {
-      const DevGemm& dg = G(dgr[l]);
-      for (int i = 0; i < TM; ++i)
-        for (int j = 0; j < dg.tiles_n; ++j) {
-          pkt_task t = gemm_task(dgr[l], i, j);
-          t.header.buffer_read_id = uint16_t(Bk[l][i]);
-          t.header.wait_count = uint32_t(dy_tn[l]);
-          t.header.buffer_write_id = uint16_t(Bk[l - 1][i]);
-          t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
-          tl.push_back(t);
-          ++tiles;
-        }
-    }
     const DevGemm& wg = G(wgr[l]);
     for (int i = 0; i < wg.tiles_m; ++i)
       for (int j = 0; j < wg.tiles_n; ++j) {
@@ -416,7 +429,7 @@ int Mlp::build(int p, int q) {
         t.header.opcode = PKT_OP_BIAS_SGD;
         pkt_bias_sgd_args a{};
         a.partials = colsum[l];
-        a.num_partials = TM;
+        a.num_partials = TMr;
         a.ld = ld[l + 1];
         a.col_begin = c0;
         a.col_end = std::min(n, c0 + 512);
@@ -515,8 +528,8 @@ int Mlp::launch_list(pkt_task* d, int n, cudaStream_t st) {
     }
     kp.perf = rt->d_perf;
   }
-  rt->last_blocks = rt->num_sms;
-  e = launch_megakernel(kp, rt->num_sms, st);
+  rt->last_blocks = rt->num_sms & ~(P - 1);
+  e = launch_megakernel(kp, rt->num_sms & ~(P - 1), st, P);
   if (e != cudaSuccess) return cuda_fail(e, "launch megakernel");
   return PKT_OK;
 }
@@ -777,6 +790,29 @@ int pkt_mlp_step_info(pkt_mlp* h, int* tasks, int* gemm_tiles, double* flops) {
   if (tasks) *tasks = int(h->m->tasks[0][0].size() + h->m->update[0].size());
   if (gemm_tiles) *gemm_tiles = h->m->gemm_tiles_per_step;
   if (flops) *flops = h->m->flops_per_step;
+  return PKT_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int pkt_mlp_set_perf(pkt_mlp* h, int enabled) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  h->m->rt->perf_enabled = enabled != 0;
+  return PKT_OK;
+}
+
+int pkt_mlp_fetch_perf(pkt_mlp* h, unsigned long long* out, int max_blocks, int* blocks) {
+  if (!h || !out || !blocks) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  pkb::Runtime* rt = h->m->rt;
+  if (!rt->perf_enabled || !rt->d_perf) return pkb::fail(PKT_ERR_ARGS, "perf counters are off");
+  cudaSetDevice(rt->device);
+  const int nb = std::min(max_blocks, rt->last_blocks);
+  cudaError_t e = cudaMemcpy(out, rt->d_perf, sizeof(unsigned long long) * PKT_PERF_WORDS * nb,
+                             cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return pkb::cuda_fail(e, "read perf");
+  *blocks = nb;
   return PKT_OK;
 }
 

@@ -81,7 +81,8 @@ static int make_map(CUtensorMap* map, const void* base, int dtype, long long col
 int gemm_tiles(const pkt_gemm_desc& d, int* tm, int* tn) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0 || d.bn < 16 || d.bn > kMaxBN || d.bn % 16 != 0)
     return fail(PKT_ERR_ARGS, "GEMM shape M=%d N=%d K=%d bn=%d invalid", d.M, d.N, d.K, d.bn);
-  *tm = (d.M + kBM - 1) / kBM;
+  const int pair = d.cta_pair == 2 ? 2 : 1;
+  *tm = (d.M + kBM * pair - 1) / (kBM * pair);
   *tn = (d.N + d.bn - 1) / d.bn;
   return PKT_OK;
 }
@@ -97,6 +98,10 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
     return fail(PKT_ERR_ARGS, "GEMM out_dtype must be bf16 or f32");
   const bool bf = d.in_dtype == PKT_DTYPE_BF16;
   const int es = bf ? 2 : 4;
+  g->pair = d.cta_pair == 2 ? 2 : 1;
+  g->b_rows = d.bn / g->pair;
+  if (g->pair == 2 && (d.bn % 32 != 0))
+    return fail(PKT_ERR_ARGS, "CTA-pair tiles need bn multiple of 32 (got %d)", d.bn);
   g->bk = bf ? 64 : 32;
   g->box_mn = 128 / es;
   g->num_kb = (d.K + g->bk - 1) / g->bk;
@@ -124,18 +129,18 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
   }
   if (rc) return rc;
   if (d.b_major == PKT_MAJOR_K) {
-    rc = make_map(&g->map_b, d.b, d.in_dtype, d.K, d.N, d.ldb, g->bk, d.bn);
+    rc = make_map(&g->map_b, d.b, d.in_dtype, d.K, d.N, d.ldb, g->bk, g->b_rows);
     g->b_boxes = 1;
-    g->b_box_bytes = d.bn * 128;
+    g->b_box_bytes = g->b_rows * 128;
     g->b_lbo = 16;
     g->b_sbo = 1024;
     g->b_layout = 2;
     g->b_kstep = kinstr * es;
   } else {
-    if (d.bn % g->box_mn != 0)
-      return fail(PKT_ERR_ARGS, "MN-major B operand needs bn multiple of %d", g->box_mn);
+    if (g->b_rows % g->box_mn != 0)
+      return fail(PKT_ERR_ARGS, "MN-major B operand needs bn multiple of %d", g->box_mn * g->pair);
     rc = make_map(&g->map_b, d.b, d.in_dtype, d.N, d.K, d.ldb, g->box_mn, g->bk, !bf);
-    g->b_boxes = d.bn / g->box_mn;
+    g->b_boxes = g->b_rows / g->box_mn;
     g->b_box_bytes = g->bk * 128;
     g->b_lbo = g->b_box_bytes;
     g->b_sbo = bf ? 1024 : 512;
@@ -143,10 +148,12 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
     g->b_kstep = kinstr * 128;
   }
   if (rc) return rc;
-  g->stage_tx = g->a_boxes * g->a_box_bytes + g->b_boxes * g->b_box_bytes;
+  // bytes landing on the (leader's) full barrier per stage: both CTAs' loads in pair mode
+  g->stage_tx = g->pair * (g->a_boxes * g->a_box_bytes + g->b_boxes * g->b_box_bytes);
   const uint32_t fmt = bf ? 1u : 2u;
   g->idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(d.a_major) << 15) |
-             (uint32_t(d.b_major) << 16) | (uint32_t(d.bn >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+             (uint32_t(d.b_major) << 16) | (uint32_t(d.bn >> 3) << 17) |
+             (uint32_t((kBM * g->pair) >> 4) << 24);
   // epilogue operand checks
   if (!d.out && d.epilogue != PKT_EPI_WGRAD_SGD) return fail(PKT_ERR_ARGS, "GEMM output pointer missing");
   if ((d.epilogue == PKT_EPI_MSE || d.epilogue == PKT_EPI_DGRAD_RELU) && !d.aux)
@@ -250,13 +257,13 @@ int Runtime::launch(int blocks, cudaStream_t stream) {
   cudaSetDevice(device);
   if (blocks <= 0) blocks = num_sms;
   if (!d_state) return fail(PKT_ERR_ARGS, "runtime not initialized");
-  if (perf_enabled && blocks > perf_cap) {
+  if (perf_enabled && blocks + 1 > perf_cap) {
     cudaFree(d_perf);
-    cudaError_t e = cudaMalloc(&d_perf, sizeof(unsigned long long) * PKT_PERF_WORDS * blocks);
+    cudaError_t e = cudaMalloc(&d_perf, sizeof(unsigned long long) * PKT_PERF_WORDS * (blocks + 1));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(perf)");
-    perf_cap = blocks;
+    perf_cap = blocks + 1;
   }
-  if (perf_enabled) cudaMemsetAsync(d_perf, 0, sizeof(unsigned long long) * PKT_PERF_WORDS * blocks, stream);
+  if (perf_enabled) cudaMemsetAsync(d_perf, 0, sizeof(unsigned long long) * PKT_PERF_WORDS * perf_cap, stream);
   KParams p{};
   p.tasks = d_tasks;
   p.num_tasks = num_tasks;
@@ -268,8 +275,9 @@ int Runtime::launch(int blocks, cudaStream_t stream) {
   p.task_counter = accounting ? d_counter : nullptr;
   p.perf = perf_enabled ? d_perf : nullptr;
   p.timeout_ns = timeout_ns;
+  if (cta_pair == 2 && (blocks & 1)) ++blocks;  // clusters of two (perf buffer has blocks + 1 rows)
   last_blocks = blocks;
-  cudaError_t e = launch_megakernel(p, blocks, stream);
+  cudaError_t e = launch_megakernel(p, blocks, stream, cta_pair);
   if (e != cudaSuccess) return cuda_fail(e, "launch megakernel");
   return PKT_OK;
 }
@@ -442,6 +450,12 @@ int pkt_gemm_tiles(const pkt_gemm_desc* d, int* tiles_m, int* tiles_n) {
 int pkt_runtime_set_timeout_ns(pkt_runtime* rt, unsigned long long ns) {
   if (!rt || ns == 0) return pkb::fail(PKT_ERR_ARGS, "bad timeout");
   rt->rt->timeout_ns = ns;
+  return PKT_OK;
+}
+
+int pkt_runtime_set_cta_pair(pkt_runtime* rt, int pair) {
+  if (!rt || (pair != 1 && pair != 2)) return pkb::fail(PKT_ERR_ARGS, "cta pair must be 1 or 2");
+  rt->rt->cta_pair = pair;
   return PKT_OK;
 }
 

@@ -36,6 +36,7 @@ struct Runtime {
   unsigned long long timeout_ns = 2000000000ull;
   std::vector<int> segments;
   int segment_window = 4;
+  int cta_pair = 1;
 
   ~Runtime();
   static int create(int dev, Runtime** out);

@@ -34,7 +34,7 @@ def from_bf16_bits(h):
 
 class MLP:
     def __init__(self, dims, batch, dtype="bf16", lr=1e-3, bias=True, relu_last=False,
-                 grad_mode=0, max_bn=0, device=None):
+                 grad_mode=0, max_bn=0, cta_pair=2, device=None):
         L = _lib.load()
         self._L = L
         self.dims = list(dims)
@@ -43,7 +43,7 @@ class MLP:
         self.storage = np.uint16 if dtype == "bf16" else np.float32
         self._dims_c = (c_int * len(dims))(*dims)
         cfg = MlpConfig(len(dims) - 1, self._dims_c, batch, DTYPES[dtype], int(bias),
-                        int(relu_last), float(lr), int(grad_mode), int(max_bn))
+                        int(relu_last), float(lr), int(grad_mode), int(max_bn), int(cta_pair))
         if device is None:
             from .runtime import _current_device
             device = _current_device()
@@ -171,6 +171,21 @@ class MLP:
         code, task, detail = c_int(), c_int(), c_int()
         check(self._L.pkt_mlp_status(self._h, ctypes.byref(code), ctypes.byref(task), ctypes.byref(detail)))
         return code.value, task.value, detail.value
+
+    PERF_NAMES = ["tasks", "gemm_tiles", "ctrl_dep_wait", "ctrl_slot_wait", "load_stage_wait",
+                  "mma_full_wait", "mma_tmem_wait", "epi_tmem_wait", "epi_gemm", "epi_simt", "total", "mma_slot_wait", "mma_issue",
+                  "kblocks"]
+
+    def set_perf(self, on=True):
+        check(self._L.pkt_mlp_set_perf(self._h, int(bool(on))))
+
+    def fetch_perf(self, max_blocks=1024):
+        """Per-CTA counters of the last launch: list of dicts (cycles unless a count)."""
+        buf = (ctypes.c_ulonglong * (_lib.PERF_WORDS * max_blocks))()
+        got = c_int()
+        check(self._L.pkt_mlp_fetch_perf(self._h, ctypes.cast(buf, c_void_p), max_blocks, ctypes.byref(got)))
+        w = _lib.PERF_WORDS
+        return [dict(zip(self.PERF_NAMES, buf[i * w:i * w + len(self.PERF_NAMES)])) for i in range(got.value)]
 
     def step_info(self):
         t, g, f = c_int(), c_int(), ctypes.c_double()

@@ -180,6 +180,10 @@ class Runtime:
     def set_timeout_ns(self, ns):
         check(self._L.pkt_runtime_set_timeout_ns(self._h, int(ns)))
 
+    def set_cta_pair(self, pair):
+        """1: each CTA runs its own 128-row GEMM tiles; 2: CTA pairs share 256-row tiles."""
+        check(self._L.pkt_runtime_set_cta_pair(self._h, int(pair)))
+
     def set_task_accounting_enabled(self, enabled):
         self._accounting = bool(enabled)
         check(self._L.pkt_runtime_set_task_accounting(self._h, int(bool(enabled))))

@@ -52,6 +52,7 @@ def pad(n, m=64):
 
 def run_gemm(pk, desc, rt=None):
     rt = rt or pk.Runtime()
+    rt.set_cta_pair(2 if desc.cta_pair == 2 else 1)
     gid = rt.register_gemms([desc])[0]
     from pkt_b200.runtime import gemm_tiles, GemmTileArgs
     tm, tn = gemm_tiles(desc)
@@ -86,8 +87,31 @@ CASES = [
 ]
 
 
+PAIR_CASES = [
+    ("bf16", 512, 512, 256, 0, 0, 256),
+    ("bf16", 256, 256, 128, 0, 1, 128),
+    ("bf16", 384, 256, 320, 1, 1, 256),
+    ("bf16", 300, 130, 77, 0, 0, 32),
+    ("bf16", 4099, 1000, 3000, 0, 1, 128),
+    ("bf16", 1000, 777, 4099, 1, 1, 256),
+    ("tf32", 256, 256, 128, 0, 0, 256),
+    ("tf32", 256, 128, 96, 0, 1, 64),
+    ("tf32", 160, 128, 200, 1, 1, 128),
+    ("tf32", 4099, 10, 777, 0, 0, 32),
+]
+
+
+@pytest.mark.parametrize("case", PAIR_CASES, ids=lambda c: "pair_%s_%dx%dx%d_a%d_b%d_bn%d" % c)
+def test_gemm_store_cta_pair(pk, case):
+    _gemm_store(pk, case, 2)
+
+
 @pytest.mark.parametrize("case", CASES, ids=lambda c: "%s_%dx%dx%d_a%d_b%d_bn%d" % c)
 def test_gemm_store(pk, case):
+    _gemm_store(pk, case, 1)
+
+
+def _gemm_store(pk, case, pair):
     dt, M, N, K, am, bm, bn = case
     rng = np.random.default_rng(M * 7 + N * 3 + K)
     A = rng.standard_normal((M, K)).astype(np.float32)
@@ -105,6 +129,7 @@ def test_gemm_store(pk, case):
     d.b, d.ldb, d.b_major = b_t.data_ptr(), b_t.shape[1], bm
     d.epilogue = 0
     d.out, d.ldo, d.out_dtype = out.data_ptr(), out.shape[1], 3
+    d.cta_pair = pair
     run_gemm(pk, d)
     got = host(out)[:, :N]
     assert rel_err(got, ref) < TOL

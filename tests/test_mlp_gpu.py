@@ -37,8 +37,8 @@ def problem(dims, batch, seed, onehot=False):
     return x, t, Ws, bs
 
 
-def make(pk, dims, batch, dtype, lr, grad_mode, x, t, Ws, bs, bias=True):
-    m = pk.MLP(dims, batch, dtype=dtype, lr=lr, bias=bias, grad_mode=grad_mode)
+def make(pk, dims, batch, dtype, lr, grad_mode, x, t, Ws, bs, bias=True, cta_pair=2):
+    m = pk.MLP(dims, batch, dtype=dtype, lr=lr, bias=bias, grad_mode=grad_mode, cta_pair=cta_pair)
     m.set_params(Ws, bs if bias else None)
     m.load_batch(m.storage_array(x), m.storage_array(t))
     return m
@@ -83,12 +83,13 @@ def test_fused_sgd_step_matches_oracle(pk, cfg):
         assert rel_err(b1[l] - bs[l], ref["b"][l] - bs[l]) < TOL[dtype], ("b", l)
 
 
-@pytest.mark.parametrize("dtype,grad_mode", [("bf16", 0), ("tf32", 0), ("bf16", 1)])
-def test_loss_curve_within_one_percent(pk, dtype, grad_mode):
+@pytest.mark.parametrize("dtype,grad_mode,pair", [("bf16", 0, 2), ("tf32", 0, 2), ("bf16", 1, 2),
+                                                   ("bf16", 0, 1), ("tf32", 1, 1)])
+def test_loss_curve_within_one_percent(pk, dtype, grad_mode, pair):
     dims, batch, steps, lr = [64, 256, 256, 32], 512, 30, 0.05
     x, t, Ws, bs = problem(dims, batch, 5)
     ref = orc.mlp_train(dims, x, t, Ws, bs, lr, steps, mode=dtype)
-    m = make(pk, dims, batch, dtype, lr, grad_mode, x, t, Ws, bs)
+    m = make(pk, dims, batch, dtype, lr, grad_mode, x, t, Ws, bs, cta_pair=pair)
     m.train(steps)
     got = m.losses()
     assert len(got) == steps
