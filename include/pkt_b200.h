@@ -204,6 +204,14 @@ const char* pkt_last_error(void);
 /* ---- axpy entry point (pkt examples/axpy_example.cu) --------------------- */
 /* y = a*x + y over n floats on device memory, as one streaming task list. */
 int pkt_axpy(const float* x, float* y, float a, long long n, void* stream);
+/* Same result as pkt_axpy for callers that must not allocate device memory
+ * (no counterpart in pkt: its runtime always cudaMallocs its task list). The
+ * task list and status words live in a fixed ~192 KB array inside the library;
+ * n is limited to 67,108,864 floats (larger n: PKT_ERR_ARGS, nothing launched).
+ * Calls on one device share that array, so calls that overlap on the GPU race;
+ * order them on one stream. The first call on a device looks up the array's
+ * address and should come before any stream capture. */
+int pkt_axpy_noalloc(const float* x, float* y, float a, long long n, void* stream);
 
 /* ---- MLP training engine (the hot path) -------------------------------- */
 typedef struct pkt_mlp pkt_mlp;

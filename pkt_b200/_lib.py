@@ -83,6 +83,7 @@ _SIGS = {
     "pkt_runtime_fetch_perf": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
     "pkt_runtime_last_launch_blocks": ([_P], c_int),
     "pkt_axpy": ([_P, _P, c_float, c_longlong, _P], c_int),
+    "pkt_axpy_noalloc": ([_P, _P, c_float, c_longlong, _P], c_int),
     "pkt_mlp_create": ([c_int, _P, ctypes.POINTER(_P)], c_int),
     "pkt_mlp_destroy": ([_P], c_int),
     "pkt_mlp_set_params": ([_P, _P, _P], c_int),

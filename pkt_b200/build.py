@@ -6,7 +6,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libpkt_b200.so")
-SOURCES = ["megakernel.cu", "runtime.cu", "mlp.cu", "entry.cu"]
+SOURCES = ["megakernel.cu", "runtime.cu", "mlp.cu", "entry.cu", "noalloc.cu"]
 NVCC = os.environ.get("NVCC", "nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
          "-Xcompiler", "-fPIC", "-shared", "-diag-suppress", "1160"]

@@ -251,3 +251,9 @@ def _current_device():
     except Exception:
         pass
     return 0
+
+
+def axpy_noalloc(x_ptr, y_ptr, a, n, stream=None):
+    """pkt_axpy for callers that must not allocate: scratch in a fixed array of the
+    library (n <= 67,108,864); calls that overlap on the GPU race on that array."""
+    check(_lib.load().pkt_axpy_noalloc(x_ptr, y_ptr, float(a), int(n), stream))
