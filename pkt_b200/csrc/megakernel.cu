@@ -79,6 +79,9 @@ __device__ void set_error(const KParams& p, int code, int task, int detail) {
 // waiting for the controller's next task, which may itself be waiting on a
 // dependency with the same budget) get four budgets plus one second, so the
 // controller's dependency timeout is the one reported.
+// Cycle stamp for the optional per-role counters; zero (and free) when they are off.
+__device__ __forceinline__ long long stamp(bool on) { return on ? clock64() : 0; }
+
 template <bool CL = false>
 __device__ __forceinline__ bool try_wait_scoped(uint64_t* bar, uint32_t parity) {
   return CL ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
@@ -257,44 +260,52 @@ __device__ void loader_loop(const KParams& p, SmemT<P>& s, uint32_t rank, unsign
     // rows [rank*bn/2, +bn/2) of B; both CTAs' bytes count on the leader's barrier
     const int m0 = int(ga.tile_m) * kBM * P + int(rank) * kBM;
     const int n0 = int(ga.tile_n) * g.d.bn + int(rank) * g.b_rows;
+    // per-tile constants in registers (the asm "memory" clobbers would force reloads)
+    const int num_kb = g.num_kb, bk = g.bk, box_mn = g.box_mn;
+    const int a_boxes = g.d.a_major == PKT_MAJOR_K ? 0 : g.a_boxes;  // 0: one K-major box
+    const int b_boxes = g.d.b_major == PKT_MAJOR_K ? 0 : g.b_boxes;
+    const uint32_t a_box_bytes = g.a_box_bytes, b_box_bytes = g.b_box_bytes, stage_tx = g.stage_tx;
+    const void* map_a = &g.map_a;
+    const void* map_b = &g.map_b;
     bool ok = true;
-    for (int kb = 0; kb < g.num_kb; ++kb) {
-      const long long c0 = clock64();
-      if (!wait_bar<(P == 2)>(p, &s.empty[stage], phase ^ 1, 4)) {
+    const bool prof = perf != nullptr;
+    for (int kb = 0; kb < num_kb; ++kb) {
+      const long long c0 = stamp(prof);
+      if (!wait_bar(p, &s.empty[stage], phase ^ 1, 4)) {
         ok = false;
         break;
       }
-      wait_cycles += clock64() - c0;
-      if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], g.stage_tx);
+      wait_cycles += stamp(prof) - c0;
+      if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], stage_tx);
       uint8_t* sa = s.stages[stage];
       uint8_t* sb = s.stages[stage] + kATileBytes;
-      const int k0 = kb * g.bk;
+      const int k0 = kb * bk;
       if (P == 1) {
-        if (g.d.a_major == PKT_MAJOR_K) {
-          tma_load_2d(sa, &g.map_a, &s.full[stage], k0, m0);
+        if (a_boxes == 0) {
+          tma_load_2d(sa, map_a, &s.full[stage], k0, m0);
         } else {
-          for (int i = 0; i < g.a_boxes; ++i)
-            tma_load_2d(sa + i * g.a_box_bytes, &g.map_a, &s.full[stage], m0 + i * g.box_mn, k0);
+          for (int i = 0; i < a_boxes; ++i)
+            tma_load_2d(sa + i * a_box_bytes, map_a, &s.full[stage], m0 + i * box_mn, k0);
         }
-        if (g.d.b_major == PKT_MAJOR_K) {
-          tma_load_2d(sb, &g.map_b, &s.full[stage], k0, n0);
+        if (b_boxes == 0) {
+          tma_load_2d(sb, map_b, &s.full[stage], k0, n0);
         } else {
-          for (int i = 0; i < g.b_boxes; ++i)
-            tma_load_2d(sb + i * g.b_box_bytes, &g.map_b, &s.full[stage], n0 + i * g.box_mn, k0);
+          for (int i = 0; i < b_boxes; ++i)
+            tma_load_2d(sb + i * b_box_bytes, map_b, &s.full[stage], n0 + i * box_mn, k0);
         }
       } else {
         const uint32_t fb = mapa_shared(smem_u32(&s.full[stage]), 0);  // leader's barrier
-        if (g.d.a_major == PKT_MAJOR_K) {
-          tma_load_2d_pair(sa, &g.map_a, fb, k0, m0);
+        if (a_boxes == 0) {
+          tma_load_2d_pair(sa, map_a, fb, k0, m0);
         } else {
-          for (int i = 0; i < g.a_boxes; ++i)
-            tma_load_2d_pair(sa + i * g.a_box_bytes, &g.map_a, fb, m0 + i * g.box_mn, k0);
+          for (int i = 0; i < a_boxes; ++i)
+            tma_load_2d_pair(sa + i * a_box_bytes, map_a, fb, m0 + i * box_mn, k0);
         }
-        if (g.d.b_major == PKT_MAJOR_K) {
-          tma_load_2d_pair(sb, &g.map_b, fb, k0, n0);
+        if (b_boxes == 0) {
+          tma_load_2d_pair(sb, map_b, fb, k0, n0);
         } else {
-          for (int i = 0; i < g.b_boxes; ++i)
-            tma_load_2d_pair(sb + i * g.b_box_bytes, &g.map_b, fb, n0 + i * g.box_mn, k0);
+          for (int i = 0; i < b_boxes; ++i)
+            tma_load_2d_pair(sb + i * b_box_bytes, map_b, fb, n0 + i * box_mn, k0);
         }
       }
       ++issued;
@@ -343,40 +354,49 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
     if (op == kOpStop) break;
     if (op != PKT_OP_GEMM) continue;
     const DevGemm& g = p.gemms[ga.gemm];
+    // Everything the issue loop needs goes to registers once per tile: the
+    // "memory" clobber of each tcgen05.mma would otherwise make the compiler
+    // reload these fields from global memory between MMAs and starve the pipe.
+    const int num_kb = g.num_kb;
+    const uint32_t idesc = g.idesc;
+    const uint32_t a_kstep = g.a_kstep, b_kstep = g.b_kstep;
+    const uint64_t a_hi = smem_desc(0, g.a_lbo, g.a_sbo, g.a_layout);
+    const uint64_t b_hi = smem_desc(0, g.b_lbo, g.b_sbo, g.b_layout);
+    const bool tf32 = g.d.in_dtype == PKT_DTYPE_TF32;
     const uint32_t acc = gemm_count & 1, use = gemm_count >> 1;
     const long long c0 = clock64();
     if (!wait_bar<(P == 2)>(p, &s.tmem_empty[acc], (use & 1) ^ 1, 6)) break;
     tmem_wait += clock64() - c0;
     tc_fence_after();
     const uint32_t d_tmem = tmem_base + acc * 256;
-    const bool tf32 = g.d.in_dtype == PKT_DTYPE_TF32;
     bool ok = true;
-    for (int kb = 0; kb < g.num_kb; ++kb) {
-      const long long c1 = clock64();
-      if (!wait_bar<(P == 2)>(p, &s.full[stage], phase, 7)) {
+    const bool prof = perf != nullptr;
+    for (int kb = 0; kb < num_kb; ++kb) {
+      const long long c1 = stamp(prof);
+      if (!wait_bar(p, &s.full[stage], phase, 7)) {
         ok = false;
         break;
       }
-      const long long c2 = clock64();
+      const long long c2 = stamp(prof);
       full_wait += c2 - c1;
       tc_fence_after();
       const uint32_t sa = smem_u32(s.stages[stage]);
       const uint32_t sb = sa + kATileBytes;
-#pragma unroll 1
-      for (int k = 0; k < g.mma_per_kb; ++k) {
-        const uint64_t ad = smem_desc(sa + k * g.a_kstep, g.a_lbo, g.a_sbo, g.a_layout);
-        const uint64_t bd = smem_desc(sb + k * g.b_kstep, g.b_lbo, g.b_sbo, g.b_layout);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {  // 4 MMAs per 128-byte K block (bf16 K=16, tf32 K=8)
+        const uint64_t ad = a_hi | uint64_t(((sa + k * a_kstep) >> 4) & 0x3FFFu);
+        const uint64_t bd = b_hi | uint64_t(((sb + k * b_kstep) >> 4) & 0x3FFFu);
         const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
         if (P == 2) {
           if (tf32)
-            mma_tf32_pair(d_tmem, ad, bd, g.idesc, accum);
+            mma_tf32_pair(d_tmem, ad, bd, idesc, accum);
           else
-            mma_bf16_pair(d_tmem, ad, bd, g.idesc, accum);
+            mma_bf16_pair(d_tmem, ad, bd, idesc, accum);
         } else {
           if (tf32)
-            mma_tf32(d_tmem, ad, bd, g.idesc, accum);
+            mma_tf32(d_tmem, ad, bd, idesc, accum);
           else
-            mma_bf16(d_tmem, ad, bd, g.idesc, accum);
+            mma_bf16(d_tmem, ad, bd, idesc, accum);
         }
       }
       any_mma = true;
@@ -385,7 +405,7 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
         mma_commit_pair_both(&s.empty[stage]);
       else
         mma_commit(&s.empty[stage]);
-      issue += clock64() - c2;
+      issue += stamp(prof) - c2;
       ++kblocks;
       if (++stage == NST) {
         stage = 0;
@@ -540,7 +560,7 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
                               uint32_t use, unsigned long long& tmem_wait) {
   const pkt_gemm_desc& d = g.d;
   const long long c0 = clock64();
-  wait_bar<(P == 2)>(p, &s.tmem_full[acc], use & 1, 8);
+  wait_bar(p, &s.tmem_full[acc], use & 1, 8);
   tmem_wait += clock64() - c0;
   __syncwarp();  // tcgen05.ld is warp-collective
   tc_fence_after();

@@ -526,6 +526,7 @@ int Mlp::launch_list(pkt_task* d, int n, cudaStream_t st) {
       if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(perf)");
       rt->perf_cap = rt->num_sms;
     }
+    cudaMemsetAsync(rt->d_perf, 0, sizeof(unsigned long long) * PKT_PERF_WORDS * rt->perf_cap, st);
     kp.perf = rt->d_perf;
   }
   rt->last_blocks = rt->num_sms & ~(P - 1);
