@@ -68,7 +68,7 @@ constexpr int kMmaWarp = 2;
 constexpr int kEpiWarp0 = 3;
 constexpr int kEpiThreads = 128;
 constexpr int kStages = 4;       // single-CTA mode: 48 KB stages
-constexpr int kStagesPair = 6;   // pair mode: 32 KB stages (A 16 KB + half of B)
+constexpr int kStagesPair = 3;   // pair mode: 64 KB stages (A 128x128 + half of B, K depth 128 bf16)
 constexpr int kSlots = 4;
 constexpr int kBM = 128;
 constexpr int kMaxBN = 256;
@@ -89,7 +89,9 @@ struct alignas(128) DevGemm {
   int box_mn;              // elements per 128-byte row (MN-major box width)
   uint32_t stage_tx;       // bytes landed per stage
   uint32_t a_lbo, b_lbo;   // descriptor leading-byte offsets
-  uint32_t a_kstep, b_kstep;  // descriptor start advance per MMA (bytes)
+  uint32_t a_kstep, b_kstep;  // descriptor start advance per MMA within a 4-MMA K group (bytes)
+  uint32_t a_kgroup, b_kgroup;  // descriptor start advance per 4-MMA K group (bytes)
+  int kchunks;                // 128-byte K chunks per stage (1 single-CTA, 2 pair)
   uint32_t a_box_bytes, b_box_bytes;
   int pair;                     // 1: single CTA tiles (128 rows), 2: CTA-pair tiles (256 rows)
   int b_rows;                   // rows of B (N direction) each CTA loads: bn / pair

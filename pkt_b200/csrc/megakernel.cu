@@ -36,7 +36,8 @@ namespace {
 template <int P>
 struct SmemT {
   static constexpr int NST = P == 2 ? kStagesPair : kStages;
-  static constexpr int SB = P == 2 ? kATileBytes + kBTileBytes / 2 : kStageBytes;
+  static constexpr int A_BYTES = P * kATileBytes;  // pair: two 128-byte K chunks of A
+  static constexpr int SB = P == 2 ? A_BYTES + kBTileBytes : kStageBytes;
   uint8_t stages[NST][SB];  // 1024-byte aligned (kernel aligns the base)
   pkt_task slots[kSlots];
   uint64_t full[NST];
@@ -262,8 +263,9 @@ __device__ void loader_loop(const KParams& p, SmemT<P>& s, uint32_t rank, unsign
     const int n0 = int(ga.tile_n) * g.d.bn + int(rank) * g.b_rows;
     // per-tile constants in registers (the asm "memory" clobbers would force reloads)
     const int num_kb = g.num_kb, bk = g.bk, box_mn = g.box_mn;
-    const int a_boxes = g.d.a_major == PKT_MAJOR_K ? 0 : g.a_boxes;  // 0: one K-major box
-    const int b_boxes = g.d.b_major == PKT_MAJOR_K ? 0 : g.b_boxes;
+    const bool a_kmaj = g.d.a_major == PKT_MAJOR_K, b_kmaj = g.d.b_major == PKT_MAJOR_K;
+    const int a_boxes = g.a_boxes, b_boxes = g.b_boxes;
+    const int kbox = 128 / (g.d.in_dtype == PKT_DTYPE_BF16 ? 2 : 4);  // K elements per K-major box
     const uint32_t a_box_bytes = g.a_box_bytes, b_box_bytes = g.b_box_bytes, stage_tx = g.stage_tx;
     const void* map_a = &g.map_a;
     const void* map_b = &g.map_b;
@@ -278,35 +280,24 @@ __device__ void loader_loop(const KParams& p, SmemT<P>& s, uint32_t rank, unsign
       wait_cycles += stamp(prof) - c0;
       if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], stage_tx);
       uint8_t* sa = s.stages[stage];
-      uint8_t* sb = s.stages[stage] + kATileBytes;
+      uint8_t* sb = s.stages[stage] + SmemT<P>::A_BYTES;
       const int k0 = kb * bk;
+      // K-major: one box per 128-byte K chunk; MN-major: one box per 128-byte MN chunk
       if (P == 1) {
-        if (a_boxes == 0) {
-          tma_load_2d(sa, map_a, &s.full[stage], k0, m0);
-        } else {
-          for (int i = 0; i < a_boxes; ++i)
-            tma_load_2d(sa + i * a_box_bytes, map_a, &s.full[stage], m0 + i * box_mn, k0);
-        }
-        if (b_boxes == 0) {
-          tma_load_2d(sb, map_b, &s.full[stage], k0, n0);
-        } else {
-          for (int i = 0; i < b_boxes; ++i)
-            tma_load_2d(sb + i * b_box_bytes, map_b, &s.full[stage], n0 + i * box_mn, k0);
-        }
+        for (int i = 0; i < a_boxes; ++i)
+          tma_load_2d(sa + i * a_box_bytes, map_a, &s.full[stage], a_kmaj ? k0 + i * kbox : m0 + i * box_mn,
+                      a_kmaj ? m0 : k0);
+        for (int i = 0; i < b_boxes; ++i)
+          tma_load_2d(sb + i * b_box_bytes, map_b, &s.full[stage], b_kmaj ? k0 + i * kbox : n0 + i * box_mn,
+                      b_kmaj ? n0 : k0);
       } else {
         const uint32_t fb = mapa_shared(smem_u32(&s.full[stage]), 0);  // leader's barrier
-        if (a_boxes == 0) {
-          tma_load_2d_pair(sa, map_a, fb, k0, m0);
-        } else {
-          for (int i = 0; i < a_boxes; ++i)
-            tma_load_2d_pair(sa + i * a_box_bytes, map_a, fb, m0 + i * box_mn, k0);
-        }
-        if (b_boxes == 0) {
-          tma_load_2d_pair(sb, map_b, fb, k0, n0);
-        } else {
-          for (int i = 0; i < b_boxes; ++i)
-            tma_load_2d_pair(sb + i * b_box_bytes, map_b, fb, n0 + i * box_mn, k0);
-        }
+        for (int i = 0; i < a_boxes; ++i)
+          tma_load_2d_pair(sa + i * a_box_bytes, map_a, fb, a_kmaj ? k0 + i * kbox : m0 + i * box_mn,
+                           a_kmaj ? m0 : k0);
+        for (int i = 0; i < b_boxes; ++i)
+          tma_load_2d_pair(sb + i * b_box_bytes, map_b, fb, b_kmaj ? k0 + i * kbox : n0 + i * box_mn,
+                           b_kmaj ? n0 : k0);
       }
       ++issued;
       if (++stage == NST) {
@@ -341,6 +332,9 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
   int seq = 0;
   uint32_t stage = 0, phase = 0, gemm_count = 0;
   unsigned long long full_wait = 0, tmem_wait = 0, tiles = 0, slot_wait = 0, issue = 0, kblocks = 0;
+  unsigned long long gap = 0;
+  long long tile_end = 0;
+  const long long life0 = stamp(perf != nullptr);
   bool any_mma = false;
   while (true) {
     const int slot = seq % kSlots;
@@ -360,6 +354,7 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
     const int num_kb = g.num_kb;
     const uint32_t idesc = g.idesc;
     const uint32_t a_kstep = g.a_kstep, b_kstep = g.b_kstep;
+    const uint32_t a_kgroup = g.a_kgroup, b_kgroup = g.b_kgroup;
     const uint64_t a_hi = smem_desc(0, g.a_lbo, g.a_sbo, g.a_layout);
     const uint64_t b_hi = smem_desc(0, g.b_lbo, g.b_sbo, g.b_layout);
     const bool tf32 = g.d.in_dtype == PKT_DTYPE_TF32;
@@ -371,6 +366,7 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
     const uint32_t d_tmem = tmem_base + acc * 256;
     bool ok = true;
     const bool prof = perf != nullptr;
+    if (prof && tile_end != 0) gap += clock64() - tile_end;
     for (int kb = 0; kb < num_kb; ++kb) {
       const long long c1 = stamp(prof);
       if (!wait_bar(p, &s.full[stage], phase, 7)) {
@@ -381,11 +377,13 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
       full_wait += c2 - c1;
       tc_fence_after();
       const uint32_t sa = smem_u32(s.stages[stage]);
-      const uint32_t sb = sa + kATileBytes;
+      const uint32_t sb = sa + SmemT<P>::A_BYTES;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {  // 4 MMAs per 128-byte K block (bf16 K=16, tf32 K=8)
-        const uint64_t ad = a_hi | uint64_t(((sa + k * a_kstep) >> 4) & 0x3FFFu);
-        const uint64_t bd = b_hi | uint64_t(((sb + k * b_kstep) >> 4) & 0x3FFFu);
+      for (int k = 0; k < 4 * P; ++k) {  // 4 MMAs per 128-byte K chunk (bf16 K=16, tf32 K=8)
+        const uint32_t ao = (k >> 2) * a_kgroup + (k & 3) * a_kstep;
+        const uint32_t bo = (k >> 2) * b_kgroup + (k & 3) * b_kstep;
+        const uint64_t ad = a_hi | uint64_t(((sa + ao) >> 4) & 0x3FFFu);
+        const uint64_t bd = b_hi | uint64_t(((sb + bo) >> 4) & 0x3FFFu);
         const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
         if (P == 2) {
           if (tf32)
@@ -419,6 +417,7 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
       mma_commit(&s.tmem_full[acc]);
     ++gemm_count;
     ++tiles;
+    tile_end = stamp(perf != nullptr);
   }
   if (any_mma) {
     // Every MMA this thread issued has finished before TMEM is released.
@@ -438,6 +437,8 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
     perf[kPerfMmaSlotWait] = slot_wait;
     perf[kPerfMmaIssue] = issue;
     perf[kPerfKBlocks] = kblocks;
+    perf[14] = gap;                      // from one tile's last commit to the next tile's k loop
+    perf[15] = clock64() - life0;        // MMA issuer lifetime
   }
 }
 

@@ -102,20 +102,25 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
   g->b_rows = d.bn / g->pair;
   if (g->pair == 2 && (d.bn % 32 != 0))
     return fail(PKT_ERR_ARGS, "CTA-pair tiles need bn multiple of 32 (got %d)", d.bn);
-  g->bk = bf ? 64 : 32;
+  // K depth per stage: one 128-byte chunk per CTA-stage in single mode, two in pair
+  // mode (8 MMAs per barrier round trip)
+  g->kchunks = g->pair;
+  g->bk = (bf ? 64 : 32) * g->kchunks;
   g->box_mn = 128 / es;
   g->num_kb = (d.K + g->bk - 1) / g->bk;
-  g->mma_per_kb = 4;  // bf16: K=16 per MMA, tf32: K=8 per MMA
+  g->mma_per_kb = 4 * g->kchunks;  // bf16: K=16 per MMA, tf32: K=8 per MMA
   const int kinstr = bf ? 16 : 8;
   // A operand: 128 rows of the tile.
   if (d.a_major == PKT_MAJOR_K) {
-    rc = make_map(&g->map_a, d.a, d.in_dtype, d.K, d.M, d.lda, g->bk, kBM);
+    rc = make_map(&g->map_a, d.a, d.in_dtype, d.K, d.M, d.lda, 128 / es, kBM);
     g->a_boxes = 1;
     g->a_box_bytes = kBM * 128;
     g->a_lbo = 16;
     g->a_sbo = 1024;
     g->a_layout = 2;
     g->a_kstep = kinstr * es;
+    g->a_kgroup = g->a_box_bytes;  // next 128-byte K chunk = next box
+    g->a_boxes = g->kchunks;
   } else {
     // MN-major: boxes of 128 bytes along M x bk rows of K. TF32 needs the
     // 32-byte-atom swizzle (4-row pattern, 512-byte K groups).
@@ -126,16 +131,19 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
     g->a_sbo = bf ? 1024 : 512;
     g->a_layout = bf ? 2 : 1;
     g->a_kstep = kinstr * 128;
+    g->a_kgroup = 4 * g->a_kstep;
   }
   if (rc) return rc;
   if (d.b_major == PKT_MAJOR_K) {
-    rc = make_map(&g->map_b, d.b, d.in_dtype, d.K, d.N, d.ldb, g->bk, g->b_rows);
+    rc = make_map(&g->map_b, d.b, d.in_dtype, d.K, d.N, d.ldb, 128 / es, g->b_rows);
     g->b_boxes = 1;
     g->b_box_bytes = g->b_rows * 128;
     g->b_lbo = 16;
     g->b_sbo = 1024;
     g->b_layout = 2;
     g->b_kstep = kinstr * es;
+    g->b_kgroup = g->b_box_bytes;
+    g->b_boxes = g->kchunks;
   } else {
     if (g->b_rows % g->box_mn != 0)
       return fail(PKT_ERR_ARGS, "MN-major B operand needs bn multiple of %d", g->box_mn * g->pair);
@@ -146,6 +154,7 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
     g->b_sbo = bf ? 1024 : 512;
     g->b_layout = bf ? 2 : 1;
     g->b_kstep = kinstr * 128;
+    g->b_kgroup = 4 * g->b_kstep;
   }
   if (rc) return rc;
   // bytes landing on the (leader's) full barrier per stage: both CTAs' loads in pair mode
