@@ -18,8 +18,8 @@ struct PerfBlock {
   unsigned long long mma_slot_wait_cycles{0};
   unsigned long long mma_issue_cycles{0};
   unsigned long long kblocks{0};
-  unsigned long long reserved0{0};
-  unsigned long long reserved1{0};
+  unsigned long long mma_gap_cycles{0};       // between one tile's last MMA and the next tile's first
+  unsigned long long mma_lifetime_cycles{0};
 };
 static_assert(sizeof(PerfBlock) == 16 * 8, "one PerfBlock per PKT_PERF_WORDS row");
 }  // namespace pk
