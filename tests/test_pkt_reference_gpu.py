@@ -1,0 +1,79 @@
+"""Parity against Marco-Christiani/pkt's OWN CUDA megakernel on identical inputs.
+
+oracle/_ref/libpkt_ref.so is pkt's persistent kernel built from the reference
+sources (oracle/Makefile, `make -C oracle ref`, run by __graft_entry__.build()
+where the reference tree exists). Cases stay inside pkt's documented domain
+(oracle/pkt_harness.cu checks it before launching):
+  * axpy: bit-identical outputs (both compute one fused multiply-add);
+  * pkt's train_linear problem in its domain (batch <= 64, n <= 1024) on the
+    tcgen05 TF32 engine: every step's loss within 1% of pkt's CPU loop (the
+    golden-pinned oracle), steps >= 1 within 1% of pkt's kernel, final weights
+    within 1e-3 of pkt's kernel. (pkt's kernel was once seen reporting a wrong
+    first-step loss at n = 1024 while its later steps and weights agreed; the
+    first step is therefore checked against pkt's CPU loop.)
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+from tests._gpu import dev, host, rel_err, require_gpu  # noqa: E402
+
+REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
+                   "libpkt_ref.so")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    require_gpu()
+    if not os.path.exists(REF):
+        pytest.skip("pkt's kernel was not built here (oracle/_ref needs the reference tree)")
+    L = ctypes.CDLL(REF)
+    f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+    L.pktref_axpy.argtypes = [f32p, f32p, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.pktref_train_linear.argtypes = [f32p, f32p, f32p] + [ctypes.c_int] * 4 + [ctypes.c_float, f32p,
+                                                                                 ctypes.c_int]
+    return L
+
+
+@pytest.fixture(scope="module")
+def pk():
+    import pkt_b200
+    return pkt_b200
+
+
+def test_axpy_bit_exact_vs_pkt_kernel(ref, pk):
+    ntasks, per = 1000, 1024
+    rng = np.random.default_rng(42)
+    hx = rng.uniform(-1, 1, ntasks * per).astype(np.float32)
+    hy = rng.uniform(-1, 1, ntasks * per).astype(np.float32)
+    y_pkt = hy.copy()
+    assert ref.pktref_axpy(hx, y_pkt, 2.5, ntasks, per, 0) == 0
+    x, y = dev(hx), dev(hy)
+    pk.axpy(x.data_ptr(), y.data_ptr(), 2.5, ntasks * per)
+    assert np.array_equal(host(y), y_pkt)
+
+
+@pytest.mark.parametrize("m,n,batch,steps,lr", [(64, 128, 64, 30, 0.01), (128, 256, 32, 20, 0.01),
+                                                (256, 1024, 64, 10, 0.001)])
+def test_train_linear_vs_pkt_kernel(ref, pk, m, n, batch, steps, lr):
+    W0, x, t = orc.pkt_make_linear_data(m, n, batch)
+    W_pkt = np.ascontiguousarray(W0.copy())
+    l_pkt = np.zeros(steps, np.float32)
+    assert ref.pktref_train_linear(W_pkt, np.ascontiguousarray(x), np.ascontiguousarray(t), batch, m, n,
+                                   steps, lr, l_pkt, 0) == 0
+    _, l_cpu = orc.pkt_cpu_train_linear(W0, x, t, steps, lr)
+    eng = pk.MLP([n, m], batch, dtype="tf32", lr=lr, bias=False)
+    eng.set_params([W0])
+    eng.load_batch(eng.storage_array(x), eng.storage_array(t))
+    eng.train(steps)
+    l_b200 = eng.losses()
+    W_b200 = eng.get_params()[0][0]
+    assert np.max(np.abs(l_b200 - l_cpu) / l_cpu) < 0.01
+    assert np.max(np.abs(l_b200[1:] - l_pkt[1:]) / l_pkt[1:]) < 0.01
+    assert rel_err(W_b200, W_pkt) < 1e-3
