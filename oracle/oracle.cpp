@@ -51,11 +51,15 @@ inline float bf16_round(float f) {
   return r;
 }
 
-inline float tf32_trunc(float f) {
-  // TF32 tensor-core input: the low 13 mantissa bits are not used.
+inline float tf32_round(float f) {
+  // TF32 tensor-core input as the TMA unit produces it from fp32: round to
+  // nearest even at 10 mantissa bits (NaN / Inf passed through).
   uint32_t u;
   std::memcpy(&u, &f, 4);
-  u &= 0xffffe000u;
+  if ((u & 0x7f800000u) != 0x7f800000u) {
+    u += 0xfffu + ((u >> 13) & 1u);
+    u &= 0xffffe000u;
+  }
   float r;
   std::memcpy(&r, &u, 4);
   return r;
@@ -66,7 +70,7 @@ enum Mode : int { kFp32 = 0, kTf32 = 1, kBf16 = 2 };
 inline float store_round(int mode, float v) { return mode == kBf16 ? bf16_round(v) : v; }
 inline float operand_round(int mode, float v) {
   if (mode == kBf16) return bf16_round(v);
-  if (mode == kTf32) return tf32_trunc(v);
+  if (mode == kTf32) return tf32_round(v);
   return v;
 }
 
@@ -179,7 +183,7 @@ void orc_sgd(float* W, const float* dW, float lr, long long n) {
 //   W_l -= lr dW_l;  b_l -= lr db_l
 //
 // mode 0 (fp32): fp64 accumulation of fp32 operands (the "truth").
-// mode 1 (tf32): GEMM operands truncated to TF32, fp64 accumulation, fp32 storage.
+// mode 1 (tf32): GEMM operands rounded to TF32 (nearest even), fp64 accumulation, fp32 storage.
 // mode 2 (bf16): x, target, H, dY and the weight copy used by the GEMMs are
 //   stored as bf16; GEMMs accumulate in fp64 here (fp32 on the GPU); fp32
 //   master weights and fp32 bias.

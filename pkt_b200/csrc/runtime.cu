@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -69,7 +70,10 @@ static int make_map(CUtensorMap* map, const void* base, int dtype, long long col
   cuuint64_t strides[1] = {cuuint64_t(ld * es)};
   cuuint32_t box[2] = {cuuint32_t(box_x), cuuint32_t(box_y)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, dtype == PKT_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+  // TF32 operands: fp32 in memory, converted to TF32 by round-to-nearest as the TMA
+  // unit loads them (plain truncation by the tensor core would bias every product).
+  const CUtensorMapDataType tf32_type = CU_TENSOR_MAP_DATA_TYPE_TFLOAT32;
+  CUresult r = enc(map, dtype == PKT_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : tf32_type,
                    2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE,
                    atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,

@@ -29,8 +29,10 @@ def bf16r(a):
 
 
 def tf32r(a):
-    u = np.ascontiguousarray(a, np.float32).view(np.uint32) & np.uint32(0xFFFFE000)
-    return u.view(np.float32)
+    """fp32 -> TF32 by round-to-nearest-even (what the TMA loads feed the MMA)."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0xFFF + ((u >> 13) & 1)) & 0xFFFFE000
+    return u.astype(np.uint32).view(np.float32).reshape(np.shape(a))
 
 
 def stored(a, dtype, ld):
