@@ -325,6 +325,41 @@ __device__ void loader_loop(const KParams& p, SmemT<P>& s, uint32_t rank, unsign
 }
 
 // ============================================================ MMA issuer
+// One stage's MMAs (4 per 128-byte K chunk: bf16 K=16, tf32 K=8) and the commit
+// that frees the stage once they have read it. The operand type is a template
+// argument so the issue stream holds no per-MMA branch; only the first MMA of a
+// tile (acc_first == 0) overwrites the accumulator.
+template <int P, bool TF32>
+__device__ __forceinline__ void issue_kblock(uint64_t* empty_bar, uint32_t d_tmem, uint64_t a_hi,
+                                             uint64_t b_hi, uint32_t sa, uint32_t sb, uint32_t idesc,
+                                             uint32_t a_kstep, uint32_t b_kstep, uint32_t a_kgroup,
+                                             uint32_t b_kgroup, uint32_t acc_first) {
+#pragma unroll
+  for (int k = 0; k < 4 * P; ++k) {
+    const uint32_t ao = (k >> 2) * a_kgroup + (k & 3) * a_kstep;
+    const uint32_t bo = (k >> 2) * b_kgroup + (k & 3) * b_kstep;
+    const uint64_t ad = a_hi | uint64_t((sa + ao) >> 4);
+    const uint64_t bd = b_hi | uint64_t((sb + bo) >> 4);
+    const uint32_t accum = k == 0 ? acc_first : 1u;
+    if (P == 2) {
+      if (TF32)
+        mma_tf32_pair(d_tmem, ad, bd, idesc, accum);
+      else
+        mma_bf16_pair(d_tmem, ad, bd, idesc, accum);
+    } else {
+      if (TF32)
+        mma_tf32(d_tmem, ad, bd, idesc, accum);
+      else
+        mma_bf16(d_tmem, ad, bd, idesc, accum);
+    }
+  }
+  // stage reusable (in both CTAs of a pair) once these MMAs have read it
+  if (P == 2)
+    mma_commit_pair_both(empty_bar);
+  else
+    mma_commit(empty_bar);
+}
+
 template <int P>
 __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
                          unsigned long long* perf) {
@@ -336,6 +371,9 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
   long long tile_end = 0;
   const long long life0 = stamp(perf != nullptr);
   bool any_mma = false;
+  // The whole warp runs the loop (converged); one elected lane issues each
+  // tcgen05.mma / commit, as the instructions are single-thread.
+  const bool elected = (threadIdx.x & 31) == 0;
   while (true) {
     const int slot = seq % kSlots;
     const long long cs = clock64();
@@ -343,7 +381,8 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
     slot_wait += clock64() - cs;
     const uint16_t op = s.slots[slot].header.opcode;
     pkt_gemm_tile_args ga = *reinterpret_cast<const pkt_gemm_tile_args*>(s.slots[slot].args);
-    mbar_arrive(&s.slot_empty[slot]);  // the MMA issuer only runs in the leader CTA
+    if (elected) mbar_arrive(&s.slot_empty[slot]);  // the MMA issuer only runs in the leader CTA
+    __syncwarp();
     ++seq;
     if (op == kOpStop) break;
     if (op != PKT_OP_GEMM) continue;
@@ -378,31 +417,16 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
       tc_fence_after();
       const uint32_t sa = smem_u32(s.stages[stage]);
       const uint32_t sb = sa + SmemT<P>::A_BYTES;
-#pragma unroll
-      for (int k = 0; k < 4 * P; ++k) {  // 4 MMAs per 128-byte K chunk (bf16 K=16, tf32 K=8)
-        const uint32_t ao = (k >> 2) * a_kgroup + (k & 3) * a_kstep;
-        const uint32_t bo = (k >> 2) * b_kgroup + (k & 3) * b_kstep;
-        const uint64_t ad = a_hi | uint64_t(((sa + ao) >> 4) & 0x3FFFu);
-        const uint64_t bd = b_hi | uint64_t(((sb + bo) >> 4) & 0x3FFFu);
-        const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-        if (P == 2) {
-          if (tf32)
-            mma_tf32_pair(d_tmem, ad, bd, idesc, accum);
-          else
-            mma_bf16_pair(d_tmem, ad, bd, idesc, accum);
-        } else {
-          if (tf32)
-            mma_tf32(d_tmem, ad, bd, idesc, accum);
-          else
-            mma_bf16(d_tmem, ad, bd, idesc, accum);
-        }
+      if (elected) {
+        if (tf32)
+          issue_kblock<P, true>(&s.empty[stage], d_tmem, a_hi, b_hi, sa, sb, idesc, a_kstep, b_kstep,
+                                a_kgroup, b_kgroup, kb > 0 ? 1u : 0u);
+        else
+          issue_kblock<P, false>(&s.empty[stage], d_tmem, a_hi, b_hi, sa, sb, idesc, a_kstep, b_kstep,
+                                 a_kgroup, b_kgroup, kb > 0 ? 1u : 0u);
       }
+      __syncwarp();
       any_mma = true;
-      // stage reusable (in both CTAs of a pair) once these MMAs have read it
-      if (P == 2)
-        mma_commit_pair_both(&s.empty[stage]);
-      else
-        mma_commit(&s.empty[stage]);
       issue += stamp(prof) - c2;
       ++kblocks;
       if (++stage == NST) {
@@ -411,26 +435,32 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
       }
     }
     if (!ok) break;
-    if (P == 2)
-      mma_commit_pair_both(&s.tmem_full[acc]);  // accumulator complete in both CTAs
-    else
-      mma_commit(&s.tmem_full[acc]);
+    if (elected) {
+      if (P == 2)
+        mma_commit_pair_both(&s.tmem_full[acc]);  // accumulator complete in both CTAs
+      else
+        mma_commit(&s.tmem_full[acc]);
+    }
+    __syncwarp();
     ++gemm_count;
     ++tiles;
     tile_end = stamp(perf != nullptr);
   }
   if (any_mma) {
     // Every MMA this thread issued has finished before TMEM is released.
-    if (P == 2)
-      mma_commit_pair_local(&s.mma_drain);
-    else
-      mma_commit(&s.mma_drain);
+    if (elected) {
+      if (P == 2)
+        mma_commit_pair_local(&s.mma_drain);
+      else
+        mma_commit(&s.mma_drain);
+    }
+    __syncwarp();
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(&s.mma_drain, 0)) {
       if (globaltimer_ns() - t0 > p.timeout_ns) break;
     }
   }
-  if (perf) {
+  if (perf && elected) {
     perf[kPerfGemmTiles] = tiles;
     perf[kPerfMmaFullWait] = full_wait;
     perf[kPerfMmaTmemWait] = tmem_wait;
@@ -1059,7 +1089,7 @@ __global__ void __launch_bounds__(kThreads, 1) pk_megakernel(const __grid_consta
     if (lane == 0) loader_loop<P>(p, s, rank, perf);
     __syncwarp();
   } else if (warp == kMmaWarp) {
-    if (lane == 0 && rank == 0) mma_loop<P>(p, s, tmem_base, perf);
+    if (rank == 0) mma_loop<P>(p, s, tmem_base, perf);
     __syncwarp();
   } else {
     const int et = int(threadIdx.x) - kEpiWarp0 * 32;
