@@ -596,114 +596,135 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
   __syncwarp();  // tcgen05.ld is warp-collective
   tc_fence_after();
 
+  // Every descriptor field the chunk loop uses goes to registers first: the
+  // "memory" clobber of each tcgen05.ld would otherwise make the compiler
+  // reload them from global memory inside the loop.
+  const int M = d.M, N = d.N, bn = d.bn, epi = d.epilogue;
+  const int out_dtype = d.out_dtype, in_dtype = d.in_dtype;
+  void* const out = d.out;
+  const long long ldo = d.ldo, ldaux = d.ldaux, ldy = d.ldy, ldw = d.ldw;
+  const float* const bias = d.bias;
+  const bool relu = d.relu != 0;
+  const void* const aux = d.aux;
+  float* const y_out = static_cast<float*>(d.y_out);
+  const float scale = d.scale, lr = d.lr;
+  const float* const w_in = d.w_in;
+  float* const w_out = d.w_out;
+  void* const w_shadow = d.w_shadow;
   const int rblock = tile_m * P + int(c.rank);  // 128-row block of this CTA's rows
   const int row = rblock * kBM + c.q * 32 + c.lane;
-  const bool row_ok = row < d.M;
-  const int n0 = tile_n * d.bn;
-  const int nchunks = (d.bn + 31) / 32;
-  const int epi = d.epilogue;
+  const bool row_ok = row < M;
+  const int n0 = tile_n * bn;
+  const int nchunks = (bn + 31) / 32;
   const bool want_colsum = (epi == PKT_EPI_MSE || epi == PKT_EPI_DGRAD_RELU) && d.colsum != nullptr;
-  const int out_es = d.out_dtype == PKT_DTYPE_BF16 ? 2 : 4;
-  const int in_es = d.in_dtype == PKT_DTYPE_BF16 ? 2 : 4;
+  const int out_es = out_dtype == PKT_DTYPE_BF16 ? 2 : 4;
+  const int in_es = in_dtype == PKT_DTYPE_BF16 ? 2 : 4;
+  const bool add_bias = (epi == PKT_EPI_BIAS_ACT || epi == PKT_EPI_MSE) && bias != nullptr;
   float loss = 0.f;
 
+  // TMEM reads are double-buffered: chunk ch+1 is in flight while chunk ch is
+  // processed and stored.
+  const uint32_t tbase = tmem_base + (uint32_t(c.q * 32) << 16) + acc * 256;
+  uint32_t r[32];
+  tmem_ld32(tbase, r);
+  tmem_ld_wait_regs(r);
   for (int ch = 0; ch < nchunks; ++ch) {
-    uint32_t r[32];
-    const uint32_t taddr = tmem_base + (uint32_t(c.q * 32) << 16) + acc * 256 + ch * 32;
-    tmem_ld32(taddr, r);
-    tmem_ld_wait();
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    const bool more = ch + 1 < nchunks;
+    if (more) tmem_ld32(tbase + (ch + 1) * 32, r);
     const int col0 = n0 + ch * 32;
-    int nvalid = min(d.N - col0, d.bn - ch * 32);  // inside the matrix and inside this tile
+    int nvalid = min(N - col0, bn - ch * 32);  // inside the matrix and inside this tile
     nvalid = nvalid < 0 ? 0 : (nvalid > 32 ? 32 : nvalid);
     if (!row_ok) nvalid = 0;
+    // bias of the chunk's 32 columns: one coalesced load, broadcast by shuffles
+    float bl = 0.f;
+    if (add_bias && col0 + c.lane < N) bl = __ldg(bias + col0 + c.lane);
 
     if (epi == PKT_EPI_STORE || epi == PKT_EPI_WGRAD_STORE) {
-      const long long o = (long long)row * d.ldo + col0;
-      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(d.out) + o * out_es);
-      if (nvalid > 0) store_row32(d.out, d.out_dtype, o, nvalid, vec, v);
+      const long long o = (long long)row * ldo + col0;
+      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(out) + o * out_es);
+      if (nvalid > 0) store_row32(out, out_dtype, o, nvalid, vec, v);
     } else if (epi == PKT_EPI_BIAS_ACT) {
-      if (d.bias) {
+      if (add_bias) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] += (col0 + j < d.N) ? __ldg(d.bias + col0 + j) : 0.f;
+        for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bl, j);
       }
-      if (d.relu) {
+      if (relu) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
       }
-      const long long o = (long long)row * d.ldo + col0;
-      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(d.out) + o * out_es);
-      if (nvalid > 0) store_row32(d.out, d.out_dtype, o, nvalid, vec, v);
+      const long long o = (long long)row * ldo + col0;
+      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(out) + o * out_es);
+      if (nvalid > 0) store_row32(out, out_dtype, o, nvalid, vec, v);
     } else if (epi == PKT_EPI_MSE) {
-      if (d.bias) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] += (col0 + j < d.N) ? __ldg(d.bias + col0 + j) : 0.f;
-      }
-      if (d.relu) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
-      }
-      if (d.y_out != nullptr && nvalid > 0) {
-        float y[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) y[j] = v[j];
-        const long long oy = (long long)row * d.ldy + col0;
-        store_row32(d.y_out, PKT_DTYPE_F32, oy, nvalid,
-                    aligned16(reinterpret_cast<const float*>(d.y_out) + oy), y);
-      }
       float t[32];
-      const long long oa = (long long)row * d.ldaux + col0;
-      const bool avec = aligned16(reinterpret_cast<const uint8_t*>(d.aux) + oa * in_es);
+      const long long oa = (long long)row * ldaux + col0;
+      const bool avec = aligned16(reinterpret_cast<const uint8_t*>(aux) + oa * in_es);
       if (nvalid > 0) {
-        load_row32(d.aux, d.in_dtype, oa, nvalid, avec, t);
+        load_row32(aux, in_dtype, oa, nvalid, avec, t);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j) t[j] = 0.f;
+      }
+      if (add_bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bl, j);
+      }
+      if (relu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+      }
+      if (y_out != nullptr && nvalid > 0) {
+        float y[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = v[j];
+        const long long oy = (long long)row * ldy + col0;
+        store_row32(y_out, PKT_DTYPE_F32, oy, nvalid, aligned16(y_out + oy), y);
       }
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const float diff = v[j] - t[j];
         const bool ok = j < nvalid;
         loss += ok ? diff * diff : 0.f;
-        float gr = d.scale * diff;
-        if (d.relu && v[j] <= 0.f) gr = 0.f;
+        float gr = scale * diff;
+        if (relu && v[j] <= 0.f) gr = 0.f;
         v[j] = ok ? gr : 0.f;
       }
-      const long long o = (long long)row * d.ldo + col0;
-      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(d.out) + o * out_es);
-      if (nvalid > 0) store_row32(d.out, d.out_dtype, o, nvalid, vec, v);
+      const long long o = (long long)row * ldo + col0;
+      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(out) + o * out_es);
+      if (nvalid > 0) store_row32(out, out_dtype, o, nvalid, vec, v);
     } else if (epi == PKT_EPI_DGRAD_RELU) {
       float h[32];
-      const long long oa = (long long)row * d.ldaux + col0;
-      const bool avec = aligned16(reinterpret_cast<const uint8_t*>(d.aux) + oa * in_es);
+      const long long oa = (long long)row * ldaux + col0;
+      const bool avec = aligned16(reinterpret_cast<const uint8_t*>(aux) + oa * in_es);
       if (nvalid > 0) {
-        load_row32(d.aux, d.in_dtype, oa, nvalid, avec, h);
+        load_row32(aux, in_dtype, oa, nvalid, avec, h);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j) h[j] = 0.f;
       }
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = (j < nvalid && h[j] > 0.f) ? v[j] : 0.f;
-      const long long o = (long long)row * d.ldo + col0;
-      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(d.out) + o * out_es);
-      if (nvalid > 0) store_row32(d.out, d.out_dtype, o, nvalid, vec, v);
+      const long long o = (long long)row * ldo + col0;
+      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(out) + o * out_es);
+      if (nvalid > 0) store_row32(out, out_dtype, o, nvalid, vec, v);
     } else if (epi == PKT_EPI_WGRAD_SGD) {
       float w[32];
-      const long long ow = (long long)row * d.ldw + col0;
-      const bool wvec = aligned16(d.w_in + ow) && aligned16(d.w_out + ow);
+      const long long ow = (long long)row * ldw + col0;
+      const bool wvec = aligned16(w_in + ow) && aligned16(w_out + ow);
       if (nvalid > 0) {
-        load_row32(d.w_in, PKT_DTYPE_F32, ow, nvalid, wvec, w);
+        load_row32(w_in, PKT_DTYPE_F32, ow, nvalid, wvec, w);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) w[j] = fmaf(-d.lr, v[j], w[j]);
+        for (int j = 0; j < 32; ++j) w[j] = fmaf(-lr, v[j], w[j]);
         float w2[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) w2[j] = w[j];
-        store_row32(d.w_out, PKT_DTYPE_F32, ow, nvalid, wvec, w);
-        if (d.w_shadow) {
-          const bool svec = aligned16(reinterpret_cast<const uint16_t*>(d.w_shadow) + ow);
-          store_row32(d.w_shadow, PKT_DTYPE_BF16, ow, nvalid, svec, w2);
+        store_row32(w_out, PKT_DTYPE_F32, ow, nvalid, wvec, w);
+        if (w_shadow) {
+          const bool svec = aligned16(reinterpret_cast<const uint16_t*>(w_shadow) + ow);
+          store_row32(w_shadow, PKT_DTYPE_BF16, ow, nvalid, svec, w2);
         }
       }
     }
@@ -713,6 +734,7 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
       const float cs = warp_column_sums(v, c.lane);
       s.red[ch][c.q][c.lane] = cs;
     }
+    if (more) tmem_ld_wait_regs(r);
   }
   // Accumulator fully read: hand it back to the MMA warp.
   tc_fence_before();
