@@ -75,6 +75,7 @@ constexpr int kMaxBN = 256;
 constexpr int kATileBytes = kBM * 128;
 constexpr int kBTileBytes = kMaxBN * 128;
 constexpr int kStageBytes = kATileBytes + kBTileBytes;
+constexpr int kEpiStageBytes = 6144;  // per compute warp: one 32x32 chunk, fp32 (4 KB) + bf16 (2 KB)
 constexpr int kTmemCols = 512;  // two 256-column fp32 accumulators
 constexpr uint16_t kOpStop = 0xFFFF;
 
@@ -98,7 +99,12 @@ struct alignas(128) DevGemm {
   uint32_t a_sbo, b_sbo;        // descriptor stride-byte offsets
   uint32_t a_layout, b_layout;  // descriptor swizzle mode: 2 = 128B, 1 = 128B with 32B atoms
   int mma_per_kb;
-  int pad_[3];
+  int tma_out;     // 1: the epilogue writes `out` with TMA tile stores through map_out
+  int tma_w;       // 1: WGRAD_SGD writes w_out / w_shadow through map_w / map_shadow
+  int pad_[1];
+  CUtensorMap map_out;     // out: boxes of 32 columns x 32 rows (one compute warp's chunk)
+  CUtensorMap map_w;       // w_out (fp32)
+  CUtensorMap map_shadow;  // w_shadow (bf16)
 };
 
 // Per-CTA perf words (pkt_runtime_fetch_perf), cycles unless noted.

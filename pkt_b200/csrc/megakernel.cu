@@ -39,6 +39,9 @@ struct SmemT {
   static constexpr int A_BYTES = P * kATileBytes;  // pair: two 128-byte K chunks of A
   static constexpr int SB = P == 2 ? A_BYTES + kBTileBytes : kStageBytes;
   uint8_t stages[NST][SB];  // 1024-byte aligned (kernel aligns the base)
+  // per compute warp (TMEM lane quadrant): staging of one 32x32 output chunk for
+  // the TMA tile stores; every buffer starts on a 1024-byte boundary (swizzle)
+  uint8_t epi_stage[4][kEpiStageBytes];
   pkt_task slots[kSlots];
   uint64_t full[NST];
   uint64_t empty[NST];
@@ -58,6 +61,8 @@ struct SmemT {
 
 template <int P>
 constexpr int smem_bytes() { return int(sizeof(SmemT<P>)) + 1024; }
+static_assert(smem_bytes<1>() <= 227 * 1024 && smem_bytes<2>() <= 227 * 1024,
+              "shared memory layout exceeds the 227 KB a CTA can use");
 
 __device__ __forceinline__ int* tok_count(const KParams& p) { return p.state + kStateHeader; }
 __device__ __forceinline__ int* tok_epoch(const KParams& p) {
@@ -580,6 +585,36 @@ __device__ __forceinline__ void store_row32(void* base, int dtype, long long idx
   }
 }
 
+// Writes one row of a 32x32 chunk (this lane's row) into a TMA store staging
+// buffer, in the swizzled layout of the store's tensor map: bf16 rows are 64
+// bytes with their 16-byte units permuted by (row / 2) % 4 (64-byte swizzle),
+// fp32 rows 128 bytes permuted by row % 8 (128-byte swizzle). bf16 values are
+// rounded in place, as store_row32 does.
+__device__ __forceinline__ void stage_row32(uint8_t* buf, int dtype, int lane, float (&v)[32]) {
+  if (dtype == PKT_DTYPE_BF16) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      v[2 * i] = bf16_lo(pk[i]);
+      v[2 * i + 1] = bf16_hi(pk[i]);
+    }
+    uint8_t* row = buf + lane * 64;
+    const int x = (lane >> 1) & 3;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(row + ((c ^ x) << 4)) =
+          make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+  } else {
+    uint8_t* row = buf + lane * 128;
+    const int x = lane & 7;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(row + ((c ^ x) << 4)) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  }
+}
+
 __device__ __forceinline__ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
@@ -621,6 +656,28 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
   const int in_es = in_dtype == PKT_DTYPE_BF16 ? 2 : 4;
   const bool add_bias = (epi == PKT_EPI_BIAS_ACT || epi == PKT_EPI_MSE) && bias != nullptr;
   float loss = 0.f;
+  // TMA tile stores: each warp stages its 32 rows x 32 columns and one lane
+  // stores the box; rows past M / columns past N are clipped by the TMA unit.
+  const bool tma_out = g.tma_out != 0, tma_w = g.tma_w != 0;
+  uint8_t* const stg = s.epi_stage[c.q];
+  const int row0 = rblock * kBM + c.q * 32;
+  auto emit_out = [&](float (&vv)[32], int col0, int nvalid) {
+    if (tma_out) {
+      if (c.lane == 0) bulk_wait_read_all();  // previous chunk's store has read the buffer
+      __syncwarp();
+      stage_row32(stg, out_dtype, c.lane, vv);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (c.lane == 0 && row0 < M && col0 < N) {
+        tma_store_2d(&g.map_out, stg, col0, row0);
+        bulk_commit();
+      }
+    } else {
+      const long long o = (long long)row * ldo + col0;
+      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(out) + o * out_es);
+      if (nvalid > 0) store_row32(out, out_dtype, o, nvalid, vec, vv);
+    }
+  };
 
   // TMEM reads are double-buffered: chunk ch+1 is in flight while chunk ch is
   // processed and stored.
@@ -643,9 +700,7 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
     if (add_bias && col0 + c.lane < N) bl = __ldg(bias + col0 + c.lane);
 
     if (epi == PKT_EPI_STORE || epi == PKT_EPI_WGRAD_STORE) {
-      const long long o = (long long)row * ldo + col0;
-      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(out) + o * out_es);
-      if (nvalid > 0) store_row32(out, out_dtype, o, nvalid, vec, v);
+      emit_out(v, col0, nvalid);
     } else if (epi == PKT_EPI_BIAS_ACT) {
       if (add_bias) {
 #pragma unroll
@@ -655,9 +710,7 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
       }
-      const long long o = (long long)row * ldo + col0;
-      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(out) + o * out_es);
-      if (nvalid > 0) store_row32(out, out_dtype, o, nvalid, vec, v);
+      emit_out(v, col0, nvalid);
     } else if (epi == PKT_EPI_MSE) {
       float t[32];
       const long long oa = (long long)row * ldaux + col0;
@@ -692,9 +745,7 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
         if (relu && v[j] <= 0.f) gr = 0.f;
         v[j] = ok ? gr : 0.f;
       }
-      const long long o = (long long)row * ldo + col0;
-      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(out) + o * out_es);
-      if (nvalid > 0) store_row32(out, out_dtype, o, nvalid, vec, v);
+      emit_out(v, col0, nvalid);
     } else if (epi == PKT_EPI_DGRAD_RELU) {
       float h[32];
       const long long oa = (long long)row * ldaux + col0;
@@ -707,14 +758,32 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
       }
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = (j < nvalid && h[j] > 0.f) ? v[j] : 0.f;
-      const long long o = (long long)row * ldo + col0;
-      const bool vec = aligned16(reinterpret_cast<const uint8_t*>(out) + o * out_es);
-      if (nvalid > 0) store_row32(out, out_dtype, o, nvalid, vec, v);
+      emit_out(v, col0, nvalid);
     } else if (epi == PKT_EPI_WGRAD_SGD) {
       float w[32];
       const long long ow = (long long)row * ldw + col0;
       const bool wvec = aligned16(w_in + ow) && aligned16(w_out + ow);
-      if (nvalid > 0) {
+      if (tma_w) {
+        if (nvalid > 0) {
+          load_row32(w_in, PKT_DTYPE_F32, ow, nvalid, wvec, w);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = fmaf(-lr, v[j], w[j]);
+        if (c.lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        stage_row32(stg, PKT_DTYPE_F32, c.lane, w);
+        if (w_shadow) stage_row32(stg + 4096, PKT_DTYPE_BF16, c.lane, w);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (c.lane == 0 && row0 < M && col0 < N) {
+          tma_store_2d(&g.map_w, stg, col0, row0);
+          if (w_shadow) tma_store_2d(&g.map_shadow, stg + 4096, col0, row0);
+          bulk_commit();
+        }
+      } else if (nvalid > 0) {
         load_row32(w_in, PKT_DTYPE_F32, ow, nvalid, wvec, w);
 #pragma unroll
         for (int j = 0; j < 32; ++j) w[j] = fmaf(-lr, v[j], w[j]);
@@ -768,6 +837,10 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
           ((s.lossred[0] + s.lossred[1]) + s.lossred[2]) + s.lossred[3];
     }
   }
+  // The tile's TMA stores have landed in global memory before the caller
+  // publishes the tile's completion.
+  if ((tma_out || tma_w) && c.lane == 0) bulk_wait_all();
+  __syncwarp();
 }
 
 // ============================================================ SIMT ops

@@ -82,6 +82,28 @@ static int make_map(CUtensorMap* map, const void* base, int dtype, long long col
   return PKT_OK;
 }
 
+// Tensor map for the epilogue's TMA tile stores: one box = 32 columns x 32 rows
+// (the chunk one compute warp holds), swizzled (64-byte rows for bf16, 128-byte
+// rows for fp32) so the warp's row-per-lane shared-memory writes are free of
+// bank conflicts. Returns false (and the epilogue keeps its plain stores) where
+// TMA cannot address the matrix.
+static bool make_store_map(CUtensorMap* map, const void* base, int dtype, long long cols,
+                           long long rows, long long ld) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc || base == nullptr) return false;
+  const int es = dtype == PKT_DTYPE_BF16 ? 2 : 4;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * es) % 16 != 0) return false;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld * es)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dtype == PKT_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                   2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   es == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int gemm_tiles(const pkt_gemm_desc& d, int* tm, int* tn) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0 || d.bn < 16 || d.bn > kMaxBN || d.bn % 16 != 0)
     return fail(PKT_ERR_ARGS, "GEMM shape M=%d N=%d K=%d bn=%d invalid", d.M, d.N, d.K, d.bn);
@@ -174,6 +196,17 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
   if (d.epilogue == PKT_EPI_WGRAD_SGD && (!d.w_in || !d.w_out))
     return fail(PKT_ERR_ARGS, "WGRAD_SGD epilogue needs w_in / w_out");
   if (d.epilogue < 0 || d.epilogue > PKT_EPI_WGRAD_STORE) return fail(PKT_ERR_ARGS, "bad epilogue");
+  // TMA tile stores need whole 32-column chunks inside a tile (a box must not
+  // spill into the neighbouring tile's columns).
+  if (d.bn % 32 == 0) {
+    if (d.epilogue == PKT_EPI_WGRAD_SGD) {
+      g->tma_w = make_store_map(&g->map_w, d.w_out, PKT_DTYPE_F32, d.N, d.M, d.ldw) &&
+                 (d.w_shadow == nullptr ||
+                  make_store_map(&g->map_shadow, d.w_shadow, PKT_DTYPE_BF16, d.N, d.M, d.ldw));
+    } else {
+      g->tma_out = make_store_map(&g->map_out, d.out, d.out_dtype, d.N, d.M, d.ldo);
+    }
+  }
   return PKT_OK;
 }
 
