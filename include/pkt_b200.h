@@ -69,7 +69,12 @@ enum pkt_opcode {
   PKT_OP_SGD_UPDATE = 13,     /* pkt SGDUpdateArgs */
   PKT_OP_BIAS_SGD = 20,       /* pkt_bias_sgd_args: reduce column partials, update bias */
   PKT_OP_LOSS_REDUCE = 21,    /* pkt_loss_reduce_args: deterministic sum of tile partials */
-  PKT_OP_SGD_MIXED = 22       /* pkt_sgd_mixed_args: fp32 master -= lr*g, bf16 shadow write */
+  PKT_OP_SGD_MIXED = 22,      /* pkt_sgd_mixed_args: fp32 master -= lr*g, bf16 shadow write */
+  /* Fused data parallel (MLP grad_mode 2; peer memory between the ranks' GPUs): */
+  PKT_OP_DP_WAIT = 30,        /* pkt_dp_wait_args: the next step's weights of a layer have arrived */
+  PKT_OP_DP_REDUCE = 31,      /* pkt_dp_reduce_args: sum a weight tile's partials, SGD, broadcast */
+  PKT_OP_DP_BIAS_SEND = 32,   /* pkt_dp_bias_args: this rank's bias gradient to every rank */
+  PKT_OP_DP_BIAS_APPLY = 33   /* pkt_dp_bias_args: sum the ranks' bias gradients, SGD */
 };
 
 /* Args of PKT_OP_GEMM: tile (tile_m, tile_n) of registered GEMM `gemm`. */
@@ -110,6 +115,38 @@ typedef struct pkt_sgd_mixed_args {
   int pad;
 } pkt_sgd_mixed_args;
 
+/* Args of the fused data-parallel tasks. Offsets are bytes into a rank's
+ * exchange region (identical layout on every rank); the region bases of all
+ * ranks reach the kernel through the launch, not through the task. */
+typedef struct pkt_dp_wait_args {
+  int layer;
+  int tiles;           /* weight tiles of the layer (each published once per CTA of a pair) */
+} pkt_dp_wait_args;
+
+typedef struct pkt_dp_reduce_args {
+  long long master_off; /* fp32 master of the layer [rows, ld] */
+  long long wbf_off;    /* bf16 copy the next step reads [rows, ld] */
+  long long w_elem;     /* element offset of the tile: row0 * ld + col0 */
+  int layer;
+  int tile_local;       /* index among the owner's tiles (partial slots) */
+  int rows, cols;       /* valid extent of the tile */
+  int bn;               /* row stride of a partial slot (floats) */
+  int ld;
+  float lr;             /* learning rate x gradient scale */
+  int pad;
+} pkt_dp_reduce_args;
+
+typedef struct pkt_dp_bias_args {
+  const float* partials; /* SEND: [num_partials, ld] column partial sums */
+  float* bias;           /* APPLY: [n] updated in place */
+  int num_partials;
+  int ld;
+  int n;
+  int layer;
+  int bias_off;          /* float offset of the layer in a rank's bias gradient vector */
+  float lr;              /* APPLY: learning rate x gradient scale */
+} pkt_dp_bias_args;
+
 /* ---- dtypes and GEMM registration -------------------------------------- */
 #define PKT_DTYPE_BF16 1
 #define PKT_DTYPE_TF32 2 /* fp32 storage, TF32 tensor-core inputs */
@@ -124,7 +161,9 @@ enum pkt_epilogue {
   PKT_EPI_MSE = 2,        /* y = acc + bias; out = dY = scale*(y - target); loss partials */
   PKT_EPI_DGRAD_RELU = 3, /* out = acc * (aux > 0) */
   PKT_EPI_WGRAD_SGD = 4,  /* w_out = w_in - lr*acc (fp32), w_bf16 = bf16(w_out) */
-  PKT_EPI_WGRAD_STORE = 5 /* out = acc (fp32 gradient) */
+  PKT_EPI_WGRAD_STORE = 5, /* out = acc (fp32 gradient) */
+  PKT_EPI_WGRAD_PEER = 6   /* fp32 partial tile into its owner rank's exchange region
+                              (MLP grad_mode 2 only) */
 };
 
 /* One D[M,N] = sum_k A[m,k] B[n,k] problem, tiled 128 x bn. */
@@ -225,7 +264,9 @@ typedef struct pkt_mlp_config {
   int relu_last;    /* ReLU after the output layer too (0 for plain regression) */
   float lr;
   int grad_mode;    /* 0: SGD fused into the weight-gradient epilogue; 1: store fp32
-                       gradients, separate SGD pass (data parallel / inspection) */
+                       gradients, separate SGD pass (data parallel over NCCL /
+                       inspection); 2: fused data parallel over peer memory
+                       (pkt_mlp_dp_handle / pkt_mlp_dp_connect) */
   int max_bn;       /* largest tile N to use (0: 256) */
   int cta_pair;     /* 0 or 2: CTA pairs share 256-row tiles (tcgen05 cta_group::2);
                        1: every CTA computes its own 128-row tiles */
@@ -268,6 +309,20 @@ int pkt_mlp_grad_buffer(pkt_mlp* m, float** ptr, long long* count);
 int pkt_mlp_set_grad_scale(pkt_mlp* m, float scale);
 int pkt_mlp_forward_backward(pkt_mlp* m, void* stream);
 int pkt_mlp_apply_update(pkt_mlp* m, void* stream);
+/* Fused data parallel (grad_mode 2): one launch per step on every rank; the
+ * weight-gradient tiles go to their owner rank (tile index mod world) over
+ * peer memory as they finish, the owner sums the ranks' partials in rank
+ * order, applies SGD (lr x grad_scale) to its shard of the fp32 masters and
+ * writes the new bf16 weights into every rank; the next step's forward tiles of
+ * a layer start once that layer's weights have all arrived. Set-up: every rank
+ * creates its engine, exports its exchange region (pkt_mlp_dp_handle, 64 bytes
+ * of CUDA IPC handle), the caller exchanges the handles (e.g. an all-gather over
+ * torch.distributed) and passes them, in rank order, to pkt_mlp_dp_connect.
+ * world = 1 needs no handles. All ranks must run the same number of steps;
+ * a rank that stops early makes the others' waits time out (PKT_ERR_TIMEOUT). */
+#define PKT_DP_MAX_RANKS 8
+int pkt_mlp_dp_handle(pkt_mlp* m, void* handle64);
+int pkt_mlp_dp_connect(pkt_mlp* m, int rank, int world, const void* handles);
 /* Per-CTA role cycle counters of the last launch (same layout as pkt_runtime_fetch_perf). */
 int pkt_mlp_set_perf(pkt_mlp* m, int enabled);
 int pkt_mlp_fetch_perf(pkt_mlp* m, unsigned long long* out, int max_blocks, int* blocks);

@@ -100,6 +100,8 @@ _SIGS = {
     "pkt_mlp_set_output_capture": ([_P, c_int], c_int),
     "pkt_mlp_grad_buffer": ([_P, ctypes.POINTER(_P), ctypes.POINTER(c_longlong)], c_int),
     "pkt_mlp_set_grad_scale": ([_P, c_float], c_int),
+    "pkt_mlp_dp_handle": ([_P, _P], c_int),
+    "pkt_mlp_dp_connect": ([_P, c_int, c_int, _P], c_int),
     "pkt_mlp_forward_backward": ([_P, _P], c_int),
     "pkt_mlp_apply_update": ([_P, _P], c_int),
     "pkt_mlp_set_perf": ([_P, c_int], c_int),

@@ -101,7 +101,7 @@ struct alignas(128) DevGemm {
   int mma_per_kb;
   int tma_out;     // 1: the epilogue writes `out` with TMA tile stores through map_out
   int tma_w;       // 1: WGRAD_SGD writes w_out / w_shadow through map_w / map_shadow
-  int pad_[1];
+  int dp_tile_base;  // WGRAD_PEER: index of tile (0, 0) among all weight tiles of a step
   CUtensorMap map_out;     // out: boxes of 32 columns x 32 rows (one compute warp's chunk)
   CUtensorMap map_w;       // w_out (fp32)
   CUtensorMap map_shadow;  // w_shadow (bf16)
@@ -125,6 +125,24 @@ enum PerfWord {
   kPerfKBlocks = 13,       // k-blocks issued (count)
 };
 
+// Fused data parallel: every rank's exchange region (one cudaMalloc, same
+// layout everywhere; peers' regions are CUDA IPC mappings) and the offsets of
+// its parts. Counters only grow (never reset between steps): targets are
+// multiples of the step index the launch carries.
+struct DpPeers {
+  int world, rank, pair;
+  int num_layers;
+  long long slot_bytes;       // one partial tile slot: pair*128 rows x 256 floats
+  long long recv_off;         // partial slots [owned tile][source rank]
+  long long arrive_off;       // int per owned tile: partial slots written (x pair)
+  long long wready_off;       // int per layer: owner broadcasts received (x pair)
+  long long bias_recv_off;    // fp32 [2 step parities][world][bias_total]
+  long long barrive_off;      // int per layer: bias vectors received (x pair)
+  int bias_total;             // floats in one rank's bias gradient vector
+  int pad_;
+  uint8_t* base[PKT_DP_MAX_RANKS];
+};
+
 struct KParams {
   const pkt_task* tasks;
   int num_tasks;
@@ -136,6 +154,8 @@ struct KParams {
   unsigned long long* task_counter;
   unsigned long long* perf;  // [gridDim.x][PKT_PERF_WORDS] or null
   unsigned long long timeout_ns;
+  const DpPeers* dp;  // fused data parallel (null otherwise)
+  int dp_step;        // fused data-parallel steps completed before this launch
 };
 
 constexpr int kStateHeader = 8;  // ints before the token counters

@@ -117,7 +117,8 @@ __device__ __forceinline__ bool opcode_known(uint16_t op) {
   return op == PKT_OP_INVALID || op == PKT_OP_ZERO_MEMORY || op == PKT_OP_AXPY ||
          op == PKT_OP_GEMM || op == PKT_OP_LINEAR_FORWARD || op == PKT_OP_MSE_LOSS ||
          op == PKT_OP_LINEAR_BACKWARD || op == PKT_OP_SGD_UPDATE || op == PKT_OP_BIAS_SGD ||
-         op == PKT_OP_LOSS_REDUCE || op == PKT_OP_SGD_MIXED;
+         op == PKT_OP_LOSS_REDUCE || op == PKT_OP_SGD_MIXED || op == PKT_OP_DP_WAIT ||
+         op == PKT_OP_DP_REDUCE || op == PKT_OP_DP_BIAS_SEND || op == PKT_OP_DP_BIAS_APPLY;
 }
 
 __device__ __forceinline__ void copy_task(pkt_task* dst, const pkt_task* src) {
@@ -661,6 +662,24 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
   const bool tma_out = g.tma_out != 0, tma_w = g.tma_w != 0;
   uint8_t* const stg = s.epi_stage[c.q];
   const int row0 = rblock * kBM + c.q * 32;
+  // WGRAD_PEER: this thread's row of the tile's partial slot in the owner
+  // rank's exchange region (slot rows are 256 floats apart).
+  float* peer_row = nullptr;
+  int* peer_arrive = nullptr;
+  if (epi == PKT_EPI_WGRAD_PEER) {
+    const DpPeers* dp = p.dp;
+    if (dp == nullptr) {
+      set_error(p, PKT_DEV_BAD_ARGS, -1, -3);
+    } else {
+      const int t = g.dp_tile_base + tile_m * g.tiles_n + tile_n;
+      const int owner = t % dp->world, tl = t / dp->world;
+      uint8_t* ob = dp->base[owner];
+      peer_row = reinterpret_cast<float*>(ob + dp->recv_off +
+                                          ((long long)tl * dp->world + dp->rank) * dp->slot_bytes) +
+                 (long long)(int(c.rank) * kBM + c.q * 32 + c.lane) * 256;
+      peer_arrive = reinterpret_cast<int*>(ob + dp->arrive_off) + tl;
+    }
+  }
   auto emit_out = [&](float (&vv)[32], int col0, int nvalid) {
     if (tma_out) {
       if (c.lane == 0) bulk_wait_read_all();  // previous chunk's store has read the buffer
@@ -759,6 +778,12 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = (j < nvalid && h[j] > 0.f) ? v[j] : 0.f;
       emit_out(v, col0, nvalid);
+    } else if (epi == PKT_EPI_WGRAD_PEER) {
+      if (peer_row != nullptr) {
+        float4* dst = reinterpret_cast<float4*>(peer_row + ch * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
     } else if (epi == PKT_EPI_WGRAD_SGD) {
       float w[32];
       const long long ow = (long long)row * ldw + col0;
@@ -841,6 +866,13 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
   // publishes the tile's completion.
   if ((tma_out || tma_w) && c.lane == 0) bulk_wait_all();
   __syncwarp();
+  if (epi == PKT_EPI_WGRAD_PEER) {
+    // every thread's partial rows visible system-wide, then one arrive per CTA
+    // on the owner's counter for this tile
+    __threadfence_system();
+    epi_sync();
+    if (c.et == 0 && peer_arrive != nullptr) red_release_sys_add(peer_arrive, 1);
+  }
 }
 
 // ============================================================ SIMT ops
@@ -1014,6 +1046,139 @@ __device__ void op_bias_sgd(const pkt_bias_sgd_args& a, int et, int nthr) {
   }
 }
 
+// ============================================================ fused data parallel
+// Waits (one thread) until *ctr >= target, reading at system scope: the
+// counter is advanced by other GPUs through peer memory. The budget is the
+// idle one: a peer may still be finishing its previous step.
+__device__ bool dp_wait_geq(const KParams& p, const int* ctr, int target, int where) {
+  if (ld_acquire_sys(ctr) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  const uint64_t budget = 4 * p.timeout_ns + 1000000000ull;
+  uint32_t it = 0;
+  while (ld_acquire_sys(ctr) < target) {
+    __nanosleep(64);
+    if ((++it & 15u) == 0) {
+      if (*status_word(p) != 0) return false;
+      if (globaltimer_ns() - t0 > budget) {
+        set_error(p, PKT_DEV_TIMEOUT_DEPS, -1, where);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Next step's weights of one layer: every owner's broadcast of every tile of
+// the layer (one arrive per CTA of the owner's pair) has landed here.
+__device__ void op_dp_wait(const KParams& p, const EpiCtx& c, const pkt_dp_wait_args& a) {
+  const DpPeers* dp = p.dp;
+  if (c.et == 0 && dp != nullptr) {
+    const int* ctr = reinterpret_cast<const int*>(dp->base[dp->rank] + dp->wready_off) + a.layer;
+    dp_wait_geq(p, ctr, p.dp_step * a.tiles * dp->pair, 1000 + a.layer);
+  }
+  epi_sync();
+}
+
+// Owner side of one weight tile: sum the ranks' fp32 partials in rank order,
+// fp32 master -= lr * sum, and write bf16(master) into every rank's copy for the
+// next step; then one arrive per CTA on every rank's layer counter.
+__device__ void op_dp_reduce(const KParams& p, const EpiCtx& c, const pkt_dp_reduce_args& a) {
+  const DpPeers* dp = p.dp;
+  if (dp == nullptr) return;
+  uint8_t* own = dp->base[dp->rank];
+  if (c.et == 0) {
+    const int* ctr = reinterpret_cast<const int*>(own + dp->arrive_off) + a.tile_local;
+    dp_wait_geq(p, ctr, (p.dp_step + 1) * dp->world * dp->pair, 2000 + a.layer);
+  }
+  epi_sync();
+  const long long sfl = dp->slot_bytes / 4;  // floats per slot
+  const float* slots = reinterpret_cast<const float*>(own + dp->recv_off) + (long long)a.tile_local * dp->world * sfl;
+  float* master = reinterpret_cast<float*>(own + a.master_off) + a.w_elem;
+  const int cq = (a.cols + 3) / 4;
+  const int world = dp->world;
+  for (int idx = c.tid; idx < a.rows * cq; idx += c.nthr) {
+    const int r = idx / cq, c4 = (idx - r * cq) * 4;
+    const long long so = (long long)r * a.bn + c4;
+    float* m = master + (long long)r * a.ld + c4;
+    const long long we = a.w_elem + (long long)r * a.ld + c4;
+    if (c4 + 4 <= a.cols) {
+      float4 gs = __ldcg(reinterpret_cast<const float4*>(slots + so));
+      for (int src = 1; src < world; ++src) {
+        const float4 q = __ldcg(reinterpret_cast<const float4*>(slots + src * sfl + so));
+        gs.x += q.x;
+        gs.y += q.y;
+        gs.z += q.z;
+        gs.w += q.w;
+      }
+      float4 w = *reinterpret_cast<float4*>(m);
+      w.x = fmaf(-a.lr, gs.x, w.x);
+      w.y = fmaf(-a.lr, gs.y, w.y);
+      w.z = fmaf(-a.lr, gs.z, w.z);
+      w.w = fmaf(-a.lr, gs.w, w.w);
+      *reinterpret_cast<float4*>(m) = w;
+      const uint2 b = make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
+      for (int r2 = 0; r2 < world; ++r2)
+        *reinterpret_cast<uint2*>(dp->base[r2] + a.wbf_off + we * 2) = b;
+    } else {
+      for (int j = 0; j < a.cols - c4; ++j) {
+        float gs = __ldcg(slots + so + j);
+        for (int src = 1; src < world; ++src) gs += __ldcg(slots + src * sfl + so + j);
+        const float w = fmaf(-a.lr, gs, m[j]);
+        m[j] = w;
+        const uint16_t h = uint16_t(pack_bf16x2(w, 0.f) & 0xffffu);
+        for (int r2 = 0; r2 < world; ++r2)
+          *reinterpret_cast<uint16_t*>(dp->base[r2] + a.wbf_off + (we + j) * 2) = h;
+      }
+    }
+  }
+  __threadfence_system();
+  epi_sync();
+  if (c.et == 0)
+    for (int r2 = 0; r2 < world; ++r2)
+      red_release_sys_add(reinterpret_cast<int*>(dp->base[r2] + dp->wready_off) + a.layer, 1);
+}
+
+// This rank's bias gradient of one layer (column partials summed in row-block
+// order) into every rank's receive vector for this step's parity.
+__device__ void op_dp_bias_send(const KParams& p, const EpiCtx& c, const pkt_dp_bias_args& a) {
+  const DpPeers* dp = p.dp;
+  if (dp == nullptr) return;
+  const int par = p.dp_step & 1;
+  const long long off = ((long long)(par * dp->world + dp->rank)) * dp->bias_total + a.bias_off;
+  for (int col = c.tid; col < a.n; col += c.nthr) {
+    float sum = 0.f;
+    for (int pidx = 0; pidx < a.num_partials; ++pidx) sum += a.partials[(long long)pidx * a.ld + col];
+    for (int r2 = 0; r2 < dp->world; ++r2)
+      reinterpret_cast<float*>(dp->base[r2] + dp->bias_recv_off)[off + col] = sum;
+  }
+  __threadfence_system();
+  epi_sync();
+  if (c.et == 0)
+    for (int r2 = 0; r2 < dp->world; ++r2)
+      red_release_sys_add(reinterpret_cast<int*>(dp->base[r2] + dp->barrive_off) + a.layer, 1);
+}
+
+// Every rank sums the ranks' bias gradients in rank order and applies the same
+// update, so the replicated biases stay bit-identical.
+__device__ void op_dp_bias_apply(const KParams& p, const EpiCtx& c, const pkt_dp_bias_args& a) {
+  const DpPeers* dp = p.dp;
+  if (dp == nullptr) return;
+  uint8_t* own = dp->base[dp->rank];
+  if (c.et == 0) {
+    const int* ctr = reinterpret_cast<const int*>(own + dp->barrive_off) + a.layer;
+    dp_wait_geq(p, ctr, (p.dp_step + 1) * dp->world * dp->pair, 3000 + a.layer);
+  }
+  epi_sync();
+  const int par = p.dp_step & 1;
+  const float* recv = reinterpret_cast<const float*>(own + dp->bias_recv_off) +
+                      (long long)par * dp->world * dp->bias_total + a.bias_off;
+  for (int col = c.tid; col < a.n; col += c.nthr) {
+    float sum = 0.f;
+    for (int src = 0; src < dp->world; ++src) sum += __ldcg(recv + (long long)src * dp->bias_total + col);
+    a.bias[col] = fmaf(-a.lr, sum, a.bias[col]);
+  }
+}
+
 template <int P>
 __device__ void op_loss_reduce(SmemT<P>& s, const EpiCtx& c, const pkt_loss_reduce_args& a) {
   double part = 0.0;
@@ -1086,6 +1251,18 @@ __device__ void compute_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base, 
         break;
       case PKT_OP_BIAS_SGD:
         op_bias_sgd(*reinterpret_cast<const pkt_bias_sgd_args*>(task.args), c.tid, c.nthr);
+        break;
+      case PKT_OP_DP_WAIT:
+        op_dp_wait(p, c, *reinterpret_cast<const pkt_dp_wait_args*>(task.args));
+        break;
+      case PKT_OP_DP_REDUCE:
+        op_dp_reduce(p, c, *reinterpret_cast<const pkt_dp_reduce_args*>(task.args));
+        break;
+      case PKT_OP_DP_BIAS_SEND:
+        op_dp_bias_send(p, c, *reinterpret_cast<const pkt_dp_bias_args*>(task.args));
+        break;
+      case PKT_OP_DP_BIAS_APPLY:
+        op_dp_bias_apply(p, c, *reinterpret_cast<const pkt_dp_bias_args*>(task.args));
         break;
       case PKT_OP_LOSS_REDUCE:
         if (c.rank == 0) op_loss_reduce<P>(s, c, *reinterpret_cast<const pkt_loss_reduce_args*>(task.args));

@@ -45,6 +45,16 @@ __global__ void f32_to_bf16_2d(const float* src, int rows, int cols, int lds, ui
 
 inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
+// grad_mode 2: copies the fp32 master rows/cols of one weight tile from its
+// owner's exchange region (a peer mapping) into this rank's copy.
+__global__ void gather_master_tile(const float* src, float* dst, int rows, int cols, int ld) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)rows * cols;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / cols, c = i % cols;
+    dst[r * ld + c] = src[r * ld + c];
+  }
+}
+
 }  // namespace
 
 struct Mlp {
@@ -94,6 +104,20 @@ struct Mlp {
   int gemm_tiles_per_step = 0;
   double flops_per_step = 0;
 
+  // ---- fused data parallel (grad_mode 2): the exchange region holds the fp32
+  // masters, both bf16 weight copies, the partial-tile slots, the bias
+  // gradient vectors and the counters; peers map it through CUDA IPC.
+  uint8_t* region = nullptr;
+  size_t region_bytes = 0;
+  std::vector<long long> master_off, wbf_off[2];
+  std::vector<int> wg_tm, wg_tn, wg_bn, wg_base, bias_off;
+  int wg_total = 0, bias_total = 0;
+  pkb::DpPeers hdp{};
+  pkb::DpPeers* d_dp = nullptr;
+  int dp_world = 0, dp_rank = 0;  // dp_world 0: not connected yet
+  uint8_t* peer_open[PKT_DP_MAX_RANKS] = {};
+  int dp_step = 0;
+
   ~Mlp() {
     if (rt) cudaSetDevice(rt->device);
     auto F = [](void* p) { cudaFree(p); };
@@ -105,6 +129,16 @@ struct Mlp {
     }
     for (auto p : H) F(p);
     for (auto p : dY) F(p);
+    if (region) {  // weights were carved from the exchange region
+      for (int k = 0; k < 2; ++k) {
+        W32[k].clear();
+        Wbf[k].clear();
+      }
+      for (auto p : peer_open)
+        if (p) cudaIpcCloseMemHandle(p);
+      F(region);
+      F(d_dp);
+    }
     for (int k = 0; k < 2; ++k) {
       for (auto p : W32[k]) F(p);
       for (auto p : Wbf[k]) F(p);
@@ -153,6 +187,8 @@ struct Mlp {
   }
 
   int setup(const pkt_mlp_config& c);
+  int setup_dp();
+  int connect(int rank, int world, const uint8_t* handles);
   int build(int p, int q);
   int launch_list(pkt_task* d, int n, cudaStream_t st);
 };
@@ -172,7 +208,9 @@ int Mlp::setup(const pkt_mlp_config& c) {
   lr = c.lr;
   grad_mode = c.grad_mode;
   max_bn = c.max_bn > 0 ? c.max_bn : 256;
-  if (grad_mode != 0 && grad_mode != 1) return fail(PKT_ERR_ARGS, "grad_mode must be 0 or 1");
+  if (grad_mode < 0 || grad_mode > 2) return fail(PKT_ERR_ARGS, "grad_mode must be 0, 1 or 2");
+  if (grad_mode == 2 && c.dtype != PKT_DTYPE_BF16)
+    return fail(PKT_ERR_UNSUPPORTED, "fused data parallel (grad_mode 2) needs bf16 weights");
   ld.resize(L + 1);
   for (int l = 0; l <= L; ++l) ld[l] = round_up(dims[l], 64);
   P = c.cta_pair == 1 ? 1 : 2;
@@ -193,7 +231,8 @@ int Mlp::setup(const pkt_mlp_config& c) {
     W32[k].assign(L, nullptr);
     Wbf[k].assign(L, nullptr);
   }
-  for (int l = 0; l < L; ++l) {
+  if (grad_mode == 2 && (rc = setup_dp())) return rc;
+  for (int l = 0; l < L && grad_mode != 2; ++l) {
     const size_t n = size_t(dims[l + 1]) * ld[l];
     if ((rc = alloc((void**)&W32[0][l], n * 4))) return rc;
     if (!bf && (rc = alloc((void**)&W32[1][l], n * 4))) return rc;
@@ -228,6 +267,101 @@ int Mlp::setup(const pkt_mlp_config& c) {
     if ((rc = alloc((void**)&grads, size_t(o) * 4))) return rc;
   }
   for (int l = 0; l < L; ++l) flops_per_step += 2.0 * B * dims[l] * dims[l + 1] * (l > 0 ? 3 : 2);
+  return PKT_OK;
+}
+
+// Lays out and allocates the exchange region (grad_mode 2). Its size does not
+// depend on the world size: a rank owns ceil(T / world) of the T weight tiles
+// and keeps world partial slots for each, at most T + world - 1 slots.
+int Mlp::setup_dp() {
+  const int S = PKT_DP_MAX_RANKS;
+  auto a256 = [](long long x) { return (x + 255) / 256 * 256; };
+  wg_tm.assign(L, 0);
+  wg_tn.assign(L, 0);
+  wg_bn.assign(L, 0);
+  wg_base.assign(L, 0);
+  bias_off.assign(L, 0);
+  wg_total = 0;
+  bias_total = 0;
+  for (int l = 0; l < L; ++l) {
+    const int M = dims[l + 1], N = dims[l];
+    wg_bn[l] = pick_bn(M, N, true);
+    wg_tm[l] = (M + kBM * P - 1) / (kBM * P);
+    wg_tn[l] = (N + wg_bn[l] - 1) / wg_bn[l];
+    wg_base[l] = wg_total;
+    wg_total += wg_tm[l] * wg_tn[l];
+    bias_off[l] = bias_total;
+    bias_total += round_up(dims[l + 1], 4);
+  }
+  long long off = 0;
+  master_off.assign(L, 0);
+  wbf_off[0].assign(L, 0);
+  wbf_off[1].assign(L, 0);
+  for (int l = 0; l < L; ++l) {
+    const long long n = (long long)dims[l + 1] * ld[l];
+    master_off[l] = off;
+    off += a256(n * 4);
+    for (int k = 0; k < 2; ++k) {
+      wbf_off[k][l] = off;
+      off += a256(n * 2);
+    }
+  }
+  hdp = DpPeers{};
+  hdp.pair = P;
+  hdp.num_layers = L;
+  hdp.slot_bytes = (long long)P * kBM * 256 * 4;
+  hdp.recv_off = off;
+  off += (long long)(wg_total + S) * hdp.slot_bytes;
+  hdp.arrive_off = off;
+  off += a256((long long)(wg_total + S) * 4);
+  hdp.wready_off = off;
+  off += a256((long long)L * 4);
+  hdp.barrive_off = off;
+  off += a256((long long)L * 4);
+  hdp.bias_recv_off = off;
+  hdp.bias_total = bias_total;
+  off += a256((long long)2 * S * bias_total * 4);
+  region_bytes = size_t(off);
+  int rc = alloc((void**)&region, region_bytes);  // zeroed: counters start at 0
+  if (rc) return rc;
+  for (int k = 0; k < 2; ++k) {
+    W32[k].assign(L, nullptr);
+    Wbf[k].assign(L, nullptr);
+  }
+  for (int l = 0; l < L; ++l) {
+    W32[0][l] = reinterpret_cast<float*>(region + master_off[l]);
+    for (int k = 0; k < 2; ++k) Wbf[k][l] = reinterpret_cast<uint16_t*>(region + wbf_off[k][l]);
+  }
+  return PKT_OK;
+}
+
+int Mlp::connect(int rank, int world, const uint8_t* handles) {
+  if (grad_mode != 2) return fail(PKT_ERR_ARGS, "pkt_mlp_dp_connect needs grad_mode 2");
+  if (dp_world != 0) return fail(PKT_ERR_ARGS, "already connected");
+  if (world < 1 || world > PKT_DP_MAX_RANKS || rank < 0 || rank >= world)
+    return fail(PKT_ERR_ARGS, "rank %d / world %d out of range (world <= %d)", rank, world, PKT_DP_MAX_RANKS);
+  if (world > 1 && handles == nullptr) return fail(PKT_ERR_ARGS, "peer handles missing");
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) {
+      hdp.base[r] = region;
+      continue;
+    }
+    cudaIpcMemHandle_t hd;
+    std::memcpy(&hd, handles + size_t(r) * sizeof(cudaIpcMemHandle_t), sizeof(hd));
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, hd, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle(peer exchange region)");
+    peer_open[r] = static_cast<uint8_t*>(ptr);
+    hdp.base[r] = peer_open[r];
+  }
+  hdp.world = world;
+  hdp.rank = rank;
+  cudaError_t e = cudaMalloc(&d_dp, sizeof(DpPeers));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(peer table)");
+  e = cudaMemcpy(d_dp, &hdp, sizeof(DpPeers), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "copy peer table");
+  dp_world = world;
+  dp_rank = rank;
   return PKT_OK;
 }
 
@@ -315,7 +449,10 @@ int Mlp::build(int p, int q) {
     d.ldb = ld[l];
     d.b_major = PKT_MAJOR_MN;
     d.bn = pick_bn(d.M, d.N, true);
-    if (grad_mode == 0) {
+    if (grad_mode == 2) {
+      d.epilogue = PKT_EPI_WGRAD_PEER;
+      d.out = nullptr;
+    } else if (grad_mode == 0) {
       d.epilogue = PKT_EPI_WGRAD_SGD;
       d.w_in = Wmaster(l, cur);
       d.w_out = Wmaster(l, nxt);
@@ -337,6 +474,17 @@ int Mlp::build(int p, int q) {
   int rc = rt->register_gemms(g.data(), int(g.size()), &first);
   if (rc) return rc;
   auto G = [&](int idx) -> const DevGemm& { return rt->host_gemms[first + idx]; };
+  if (grad_mode == 2) {
+    // weight-gradient tiles are numbered across layers: tile t goes to rank t % world
+    for (int l = 0; l < L; ++l) {
+      DevGemm& dg = rt->host_gemms[first + wgr[l]];
+      if (dg.tiles_m != wg_tm[l] || dg.tiles_n != wg_tn[l] || dg.d.bn != wg_bn[l])
+        return fail(PKT_ERR_UNSUPPORTED, "weight tile layout differs from the exchange region's");
+      dg.dp_tile_base = wg_base[l];
+      cudaError_t e = cudaMemcpy(rt->d_gemms + first + wgr[l], &dg, sizeof(DevGemm), cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) return cuda_fail(e, "copy gemm table");
+    }
+  }
 
   // ---- tokens
   int next_id = 1;
@@ -350,6 +498,9 @@ int Mlp::build(int p, int q) {
   for (int l = 0; l < L; ++l) BF[l] = next_id++;
   const int WG_base = next_id;
   next_id += L;
+  std::vector<int> WR(L, 0);  // grad_mode 2: this step's weights of layer l have arrived
+  if (grad_mode == 2)
+    for (int l = 0; l < L; ++l) WR[l] = next_id++;
   num_tokens = next_id;
   if (num_tokens > 65535) return fail(PKT_ERR_UNSUPPORTED, "too many dependency tokens");
   // marks per row block of dY_l (and total)
@@ -367,6 +518,17 @@ int Mlp::build(int p, int q) {
     return t;
   };
   int tiles = 0;
+  if (grad_mode == 2) {
+    for (int l = 0; l < L; ++l) {
+      pkt_task t{};
+      t.header.opcode = PKT_OP_DP_WAIT;
+      pkt_dp_wait_args a{l, wg_tm[l] * wg_tn[l]};
+      t.header.arg_bytes = sizeof(a);
+      std::memcpy(t.args, &a, sizeof(a));
+      t.header.buffer_write_id = uint16_t(WR[l]);
+      tl.push_back(t);
+    }
+  }
   for (int l = 0; l < L; ++l) {
     const DevGemm& dg = G(fwd[l]);
     for (int i = 0; i < TM; ++i)
@@ -378,6 +540,10 @@ int Mlp::build(int p, int q) {
         }
         t.header.buffer_write_id = uint16_t(F[l][i]);
         if (l == L - 1) t.header.ext_ids = uint32_t(BF[L - 1]) << 16;
+        if (grad_mode == 2) {  // second read: the layer's weights of this step
+          t.header.ext_ids |= uint32_t(WR[l]);
+          t.header.ext_wait_count = 1;
+        }
         tl.push_back(t);
         ++tiles;
       }
@@ -394,51 +560,143 @@ int Mlp::build(int p, int q) {
     t.header.wait_count = uint32_t(TM * dg.tiles_n);
     tl.push_back(t);
   }
-  // The dgrad chain (the critical path) first, row block by row block; the
-  // weight-gradient tiles, which only need a complete dY_l, after it: by the time
-  // a CTA dequeues them their inputs are normally complete, so the controller
-  // rarely blocks on a token.
-  for (int l = L - 1; l >= 1; --l) {
-    const DevGemm& dg = G(dgr[l]);
-    for (int i = 0; i < TM; ++i)
-      for (int j = 0; j < dg.tiles_n; ++j) {
-        pkt_task t = gemm_task(dgr[l], i, j);
-        t.header.buffer_read_id = uint16_t(Bk[l][i]);
-        t.header.wait_count = uint32_t(dy_tn[l]);
-        t.header.buffer_write_id = uint16_t(Bk[l - 1][i]);
-        t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
-        tl.push_back(t);
-        ++tiles;
+  if (grad_mode != 2) {
+    // The dgrad chain (the critical path) first, row block by row block; the
+    // weight-gradient tiles, which only need a complete dY_l, after it: by the time
+    // a CTA dequeues them their inputs are normally complete, so the controller
+    // rarely blocks on a token.
+    for (int l = L - 1; l >= 1; --l) {
+      const DevGemm& dg = G(dgr[l]);
+      for (int i = 0; i < TM; ++i)
+        for (int j = 0; j < dg.tiles_n; ++j) {
+          pkt_task t = gemm_task(dgr[l], i, j);
+          t.header.buffer_read_id = uint16_t(Bk[l][i]);
+          t.header.wait_count = uint32_t(dy_tn[l]);
+          t.header.buffer_write_id = uint16_t(Bk[l - 1][i]);
+          t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
+          tl.push_back(t);
+          ++tiles;
+        }
+    }
+    for (int l = L - 1; l >= 0; --l) {
+      const DevGemm& wg = G(wgr[l]);
+      for (int i = 0; i < wg.tiles_m; ++i)
+        for (int j = 0; j < wg.tiles_n; ++j) {
+          pkt_task t = gemm_task(wgr[l], i, j);
+          t.header.buffer_read_id = uint16_t(BF[l]);
+          t.header.wait_count = uint32_t(TM * dy_tn[l]);
+          t.header.buffer_write_id = uint16_t(WG_base + l);
+          tl.push_back(t);
+          ++tiles;
+        }
+      if (has_bias) {
+        const int n = dims[l + 1];
+        for (int c0 = 0; c0 < n; c0 += 512) {
+          pkt_task t{};
+          t.header.opcode = PKT_OP_BIAS_SGD;
+          pkt_bias_sgd_args a{};
+          a.partials = colsum[l];
+          a.num_partials = TMr;
+          a.ld = ld[l + 1];
+          a.col_begin = c0;
+          a.col_end = std::min(n, c0 + 512);
+          if (grad_mode == 0) {
+            a.bias = bias[l];
+            a.lr = lr;
+          } else {
+            a.grad_out = grads + db_off[l];
+          }
+          t.header.arg_bytes = sizeof(a);
+          std::memcpy(t.args, &a, sizeof(a));
+          t.header.buffer_read_id = uint16_t(BF[l]);
+          t.header.wait_count = uint32_t(TM * dy_tn[l]);
+          tl.push_back(t);
+        }
       }
-  }
-  for (int l = L - 1; l >= 0; --l) {
-    const DevGemm& wg = G(wgr[l]);
-    for (int i = 0; i < wg.tiles_m; ++i)
-      for (int j = 0; j < wg.tiles_n; ++j) {
-        pkt_task t = gemm_task(wgr[l], i, j);
-        t.header.buffer_read_id = uint16_t(BF[l]);
-        t.header.wait_count = uint32_t(TM * dy_tn[l]);
-        t.header.buffer_write_id = uint16_t(WG_base + l);
-        tl.push_back(t);
-        ++tiles;
+    }
+  } else {
+    // Fused data parallel: each layer's weight-gradient tiles follow its dgrad
+    // tiles, so partial tiles start crossing to their owners early in the
+    // backward; the owner's reduce tasks of layer l+1 come after the tiles of
+    // layer l (by then every rank has usually sent its partials).
+    const float lre = lr * grad_scale;
+    const int world = dp_world > 0 ? dp_world : 1, me = dp_world > 0 ? dp_rank : 0;
+    auto reduce_tasks = [&](int l) {
+      const int M = dims[l + 1], N = dims[l], rows_t = kBM * P;
+      for (int i = 0; i < wg_tm[l]; ++i)
+        for (int j = 0; j < wg_tn[l]; ++j) {
+          const int t = wg_base[l] + i * wg_tn[l] + j;
+          if (t % world != me) continue;
+          pkt_task tk{};
+          tk.header.opcode = PKT_OP_DP_REDUCE;
+          pkt_dp_reduce_args a{};
+          a.master_off = master_off[l];
+          a.wbf_off = wbf_off[nxt][l];
+          a.w_elem = (long long)i * rows_t * ld[l] + (long long)j * wg_bn[l];
+          a.layer = l;
+          a.tile_local = t / world;
+          a.rows = std::min(rows_t, M - i * rows_t);
+          a.cols = std::min(wg_bn[l], N - j * wg_bn[l]);
+          a.bn = 256;
+          a.ld = ld[l];
+          a.lr = lre;
+          tk.header.arg_bytes = sizeof(a);
+          std::memcpy(tk.args, &a, sizeof(a));
+          tl.push_back(tk);
+        }
+    };
+    for (int l = L - 1; l >= 0; --l) {
+      if (l >= 1) {
+        const DevGemm& dg = G(dgr[l]);
+        for (int i = 0; i < TM; ++i)
+          for (int j = 0; j < dg.tiles_n; ++j) {
+            pkt_task t = gemm_task(dgr[l], i, j);
+            t.header.buffer_read_id = uint16_t(Bk[l][i]);
+            t.header.wait_count = uint32_t(dy_tn[l]);
+            t.header.buffer_write_id = uint16_t(Bk[l - 1][i]);
+            t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
+            tl.push_back(t);
+            ++tiles;
+          }
       }
-    if (has_bias) {
-      const int n = dims[l + 1];
-      for (int c0 = 0; c0 < n; c0 += 512) {
+      const DevGemm& wg = G(wgr[l]);
+      for (int i = 0; i < wg.tiles_m; ++i)
+        for (int j = 0; j < wg.tiles_n; ++j) {
+          pkt_task t = gemm_task(wgr[l], i, j);
+          t.header.buffer_read_id = uint16_t(BF[l]);
+          t.header.wait_count = uint32_t(TM * dy_tn[l]);
+          tl.push_back(t);
+          ++tiles;
+        }
+      if (has_bias) {
         pkt_task t{};
-        t.header.opcode = PKT_OP_BIAS_SGD;
-        pkt_bias_sgd_args a{};
+        t.header.opcode = PKT_OP_DP_BIAS_SEND;
+        pkt_dp_bias_args a{};
         a.partials = colsum[l];
         a.num_partials = TMr;
         a.ld = ld[l + 1];
-        a.col_begin = c0;
-        a.col_end = std::min(n, c0 + 512);
-        if (grad_mode == 0) {
-          a.bias = bias[l];
-          a.lr = lr;
-        } else {
-          a.grad_out = grads + db_off[l];
-        }
+        a.n = dims[l + 1];
+        a.layer = l;
+        a.bias_off = bias_off[l];
+        t.header.arg_bytes = sizeof(a);
+        std::memcpy(t.args, &a, sizeof(a));
+        t.header.buffer_read_id = uint16_t(BF[l]);
+        t.header.wait_count = uint32_t(TM * dy_tn[l]);
+        tl.push_back(t);
+      }
+      if (l + 1 < L) reduce_tasks(l + 1);
+    }
+    reduce_tasks(0);
+    if (has_bias) {
+      for (int l = L - 1; l >= 0; --l) {
+        pkt_task t{};
+        t.header.opcode = PKT_OP_DP_BIAS_APPLY;
+        pkt_dp_bias_args a{};
+        a.bias = bias[l];
+        a.n = dims[l + 1];
+        a.layer = l;
+        a.bias_off = bias_off[l];
+        a.lr = lre;
         t.header.arg_bytes = sizeof(a);
         std::memcpy(t.args, &a, sizeof(a));
         t.header.buffer_read_id = uint16_t(BF[l]);
@@ -519,6 +777,8 @@ int Mlp::launch_list(pkt_task* d, int n, cudaStream_t st) {
   kp.chunk = 1;
   kp.timeout_ns = rt->timeout_ns;
   kp.perf = nullptr;
+  kp.dp = d_dp;
+  kp.dp_step = dp_step;
   if (rt->perf_enabled) {
     if (rt->perf_cap < rt->num_sms) {
       cudaFree(rt->d_perf);
@@ -614,6 +874,24 @@ int pkt_mlp_get_params(pkt_mlp* h, float* W, float* b) {
   cudaSetDevice(m->rt->device);
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return pkb::cuda_fail(e, "sync");
+  if (m->grad_mode == 2 && m->dp_world > 1) {
+    // each rank updated only the master tiles it owns: fetch the others from
+    // their owners (every rank must have finished the same steps)
+    const int rows_t = pkb::kBM * m->P;
+    for (int l = 0; l < m->L; ++l)
+      for (int i = 0; i < m->wg_tm[l]; ++i)
+        for (int j = 0; j < m->wg_tn[l]; ++j) {
+          const int t = m->wg_base[l] + i * m->wg_tn[l] + j, owner = t % m->dp_world;
+          if (owner == m->dp_rank) continue;
+          const long long el = (long long)i * rows_t * m->ld[l] + (long long)j * m->wg_bn[l];
+          const float* src = reinterpret_cast<const float*>(m->hdp.base[owner] + m->master_off[l]) + el;
+          float* dst = reinterpret_cast<float*>(m->region + m->master_off[l]) + el;
+          pkb::gather_master_tile<<<64, 256>>>(src, dst, std::min(rows_t, m->dims[l + 1] - i * rows_t),
+                                               std::min(m->wg_bn[l], m->dims[l] - j * m->wg_bn[l]), m->ld[l]);
+        }
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return pkb::cuda_fail(e, "gather master shards");
+  }
   size_t wo = 0, bo = 0;
   for (int l = 0; l < m->L; ++l) {
     const int rows = m->dims[l + 1], cols = m->dims[l];
@@ -678,10 +956,13 @@ int pkt_mlp_train(pkt_mlp* h, int steps, void* stream) {
     return pkb::fail(PKT_ERR_ARGS, "loss buffer full (%d steps); call pkt_mlp_reset_losses", m->loss_cap);
   cudaSetDevice(m->rt->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (m->grad_mode == 2 && m->dp_world == 0)
+    return pkb::fail(PKT_ERR_ARGS, "grad_mode 2: call pkt_mlp_dp_connect before training");
   for (int s = 0; s < steps; ++s) {
     const int p = m->parity, q = m->active_slot;
     int rc = m->launch_list(m->d_tasks[p][q], int(m->tasks[p][q].size()), st);
     if (rc) return rc;
+    if (m->grad_mode == 2) m->dp_step++;
     if (m->grad_mode == 1) {
       rc = m->launch_list(m->d_update[p], int(m->update[p].size()), st);
       if (rc) return rc;
@@ -721,6 +1002,28 @@ int pkt_mlp_grad_buffer(pkt_mlp* h, float** ptr, long long* count) {
   *ptr = h->m->grads;
   *count = h->m->grad_count;
   return PKT_OK;
+}
+
+int pkt_mlp_dp_handle(pkt_mlp* h, void* handle64) {
+  if (!h || !handle64) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  if (m->grad_mode != 2 || !m->region) return pkb::fail(PKT_ERR_ARGS, "pkt_mlp_dp_handle needs grad_mode 2");
+  cudaSetDevice(m->rt->device);
+  cudaIpcMemHandle_t hd;
+  cudaError_t e = cudaIpcGetMemHandle(&hd, m->region);
+  if (e != cudaSuccess) return pkb::cuda_fail(e, "cudaIpcGetMemHandle(exchange region)");
+  std::memcpy(handle64, &hd, sizeof(hd));
+  return PKT_OK;
+}
+
+int pkt_mlp_dp_connect(pkt_mlp* h, int rank, int world, const void* handles) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  cudaSetDevice(m->rt->device);
+  cudaDeviceSynchronize();
+  int rc = m->connect(rank, world, static_cast<const uint8_t*>(handles));
+  if (rc) return rc;
+  return rebuild(m);  // task lists depend on which tiles this rank owns
 }
 
 int pkt_mlp_set_grad_scale(pkt_mlp* h, float scale) {

@@ -120,7 +120,8 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
   if (rc) return rc;
   if (d.in_dtype != PKT_DTYPE_BF16 && d.in_dtype != PKT_DTYPE_TF32)
     return fail(PKT_ERR_ARGS, "GEMM in_dtype must be bf16 or tf32");
-  if (d.epilogue != PKT_EPI_WGRAD_SGD && d.out_dtype != PKT_DTYPE_BF16 && d.out_dtype != PKT_DTYPE_F32)
+  if (d.epilogue != PKT_EPI_WGRAD_SGD && d.epilogue != PKT_EPI_WGRAD_PEER && d.out_dtype != PKT_DTYPE_BF16 &&
+      d.out_dtype != PKT_DTYPE_F32)
     return fail(PKT_ERR_ARGS, "GEMM out_dtype must be bf16 or f32");
   const bool bf = d.in_dtype == PKT_DTYPE_BF16;
   const int es = bf ? 2 : 4;
@@ -190,12 +191,12 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
              (uint32_t(d.b_major) << 16) | (uint32_t(d.bn >> 3) << 17) |
              (uint32_t((kBM * g->pair) >> 4) << 24);
   // epilogue operand checks
-  if (!d.out && d.epilogue != PKT_EPI_WGRAD_SGD) return fail(PKT_ERR_ARGS, "GEMM output pointer missing");
+  if (!d.out && d.epilogue != PKT_EPI_WGRAD_SGD && d.epilogue != PKT_EPI_WGRAD_PEER) return fail(PKT_ERR_ARGS, "GEMM output pointer missing");
   if ((d.epilogue == PKT_EPI_MSE || d.epilogue == PKT_EPI_DGRAD_RELU) && !d.aux)
     return fail(PKT_ERR_ARGS, "MSE / DGRAD epilogue needs aux");
   if (d.epilogue == PKT_EPI_WGRAD_SGD && (!d.w_in || !d.w_out))
     return fail(PKT_ERR_ARGS, "WGRAD_SGD epilogue needs w_in / w_out");
-  if (d.epilogue < 0 || d.epilogue > PKT_EPI_WGRAD_STORE) return fail(PKT_ERR_ARGS, "bad epilogue");
+  if (d.epilogue < 0 || d.epilogue > PKT_EPI_WGRAD_PEER) return fail(PKT_ERR_ARGS, "bad epilogue");
   // TMA tile stores need whole 32-column chunks inside a tile (a box must not
   // spill into the neighbouring tile's columns).
   if (d.bn % 32 == 0) {

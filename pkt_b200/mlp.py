@@ -142,6 +142,25 @@ class MLP:
         check(self._L.pkt_mlp_grad_buffer(self._h, ctypes.byref(p), ctypes.byref(n)))
         return p.value, n.value
 
+    # ---- fused data parallel (grad_mode 2)
+    DP_HANDLE_BYTES = 64
+
+    def dp_handle(self):
+        """This rank's exchange-region handle (CUDA IPC, 64 bytes) for its peers."""
+        buf = ctypes.create_string_buffer(self.DP_HANDLE_BYTES)
+        check(self._L.pkt_mlp_dp_handle(self._h, ctypes.cast(buf, c_void_p)))
+        return buf.raw
+
+    def dp_connect(self, rank, world, handles=None):
+        """Maps every peer's exchange region; handles: the ranks' dp_handle()
+        bytes in rank order (None for world 1)."""
+        if world > 1:
+            assert len(handles) == world and all(len(h) == self.DP_HANDLE_BYTES for h in handles)
+            buf = ctypes.create_string_buffer(b"".join(handles), self.DP_HANDLE_BYTES * world)
+            check(self._L.pkt_mlp_dp_connect(self._h, int(rank), int(world), ctypes.cast(buf, c_void_p)))
+        else:
+            check(self._L.pkt_mlp_dp_connect(self._h, int(rank), int(world), None))
+
     def set_grad_scale(self, s):
         check(self._L.pkt_mlp_set_grad_scale(self._h, float(s)))
 
