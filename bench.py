@@ -5,8 +5,10 @@ python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--c
 Default workload (N=1): the 4-layer ReLU MLP 1024->4096->4096->4096->1024, bf16
 weights/activations with fp32 accumulation and fp32 master weights, batch 8192,
 MSE, SGD lr=1e-3 (the configuration the headline metric is quoted on). N>1:
-data parallel, the same model with 8192 rows per GPU (weak scaling), fp32
-gradients all-reduced with NCCL between the backward and the update launch.
+data parallel, the same model with 8192 rows per GPU (weak scaling); by default
+(--dp fused) one launch per step on every rank, the weight-gradient tiles
+reduced inside it over peer memory (NVLink); --dp nccl: fp32 gradients
+all-reduced with NCCL between the backward and the update launch.
 One JSON line on rank 0.
 """
 import argparse
@@ -222,7 +224,8 @@ def run_ours(args, cfg_name, cfg):
     from pkt_b200.mlp import to_bf16_bits
 
     dims, B = cfg["dims"], cfg["batch"]
-    grad_mode = 1 if ws > 1 else 0
+    nccl_dp = ws > 1 and args.dp == "nccl"
+    grad_mode = (1 if nccl_dp else 2) if ws > 1 else 0
     eng = pkt_b200.MLP(dims, B, dtype=cfg["dtype"], lr=cfg["lr"], bias=True, grad_mode=grad_mode,
                        device=local)
     if ws > 1:
@@ -245,12 +248,19 @@ def run_ours(args, cfg_name, cfg):
     copy_stream = torch.cuda.Stream()
     sp = stream.cuda_stream
     grad_t = None
-    if ws > 1:
+    if nccl_dp:
         gptr, gcount = eng.grad_buffer()
         grad_t = _wrap_device_f32(gptr, gcount, local)
+    elif ws > 1:
+        # fused data parallel: exchange the ranks' peer-memory handles once
+        handles = [None] * ws
+        dist.all_gather_object(handles, eng.dp_handle())
+        eng.dp_connect(rank, ws, handles)
+        torch.cuda.synchronize()
+        dist.barrier()
 
     def step(s_ptr):
-        if ws > 1:
+        if nccl_dp:
             eng.forward_backward(s_ptr)
             with torch.cuda.stream(stream):
                 dist.all_reduce(grad_t)
@@ -258,7 +268,7 @@ def run_ours(args, cfg_name, cfg):
         else:
             eng.train(1, s_ptr)
 
-    launches_per_step = 2 if ws > 1 else 1
+    launches_per_step = 2 if nccl_dp else 1
     # ---------------- device-resident timing
     eng.load_batch_ptr(host_x[0].data_ptr(), host_t[0].data_ptr(), 0, sp)
     for _ in range(args.warmup):
@@ -370,7 +380,9 @@ def run_ours(args, cfg_name, cfg):
         "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"],
         "data": "synthetic (seeded N(0,1) inputs/targets, Kaiming-uniform weights, zero bias)",
         "config": {"workload": cfg_name + ": " + cfg["desc"], "global_batch": B * ws,
-                   "per_gpu_batch": B, "parallelism": f"dp{ws}" if ws > 1 else "single GPU",
+                   "per_gpu_batch": B,
+                   "parallelism": (f"dp{ws} ({'NCCL all-reduce' if nccl_dp else 'fused peer-memory reduce'})"
+                                   if ws > 1 else "single GPU"),
                    "l2": "no flush: every step streams > 126 MB (weights, activations, gradients "
                          "exceed L2)", "launches_per_step": launches_per_step},
         "tflops": tflops, "pct_peak_measured_sustained": 100.0 * tflops / sustained,
@@ -415,6 +427,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--dp", default="fused", choices=["fused", "nccl"],
+                    help="N>1: weight gradients reduced inside the step launch over peer memory "
+                         "(fused) or by an NCCL all-reduce between two launches (nccl)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     if args.impl == "reference":

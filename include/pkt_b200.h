@@ -72,9 +72,8 @@ enum pkt_opcode {
   PKT_OP_SGD_MIXED = 22,      /* pkt_sgd_mixed_args: fp32 master -= lr*g, bf16 shadow write */
   /* Fused data parallel (MLP grad_mode 2; peer memory between the ranks' GPUs): */
   PKT_OP_DP_WAIT = 30,        /* pkt_dp_wait_args: the next step's weights of a layer have arrived */
-  PKT_OP_DP_REDUCE = 31,      /* pkt_dp_reduce_args: sum a weight tile's partials, SGD, broadcast */
-  PKT_OP_DP_BIAS_SEND = 32,   /* pkt_dp_bias_args: this rank's bias gradient to every rank */
-  PKT_OP_DP_BIAS_APPLY = 33   /* pkt_dp_bias_args: sum the ranks' bias gradients, SGD */
+  PKT_OP_DP_BIAS_SEND = 31,   /* pkt_dp_bias_args: this rank's bias gradient to every rank */
+  PKT_OP_DP_BIAS_APPLY = 32   /* pkt_dp_bias_args: sum the ranks' bias gradients, SGD */
 };
 
 /* Args of PKT_OP_GEMM: tile (tile_m, tile_n) of registered GEMM `gemm`. */
@@ -123,19 +122,6 @@ typedef struct pkt_dp_wait_args {
   int tiles;           /* weight tiles of the layer (each published once per CTA of a pair) */
 } pkt_dp_wait_args;
 
-typedef struct pkt_dp_reduce_args {
-  long long master_off; /* fp32 master of the layer [rows, ld] */
-  long long wbf_off;    /* bf16 copy the next step reads [rows, ld] */
-  long long w_elem;     /* element offset of the tile: row0 * ld + col0 */
-  int layer;
-  int tile_local;       /* index among the owner's tiles (partial slots) */
-  int rows, cols;       /* valid extent of the tile */
-  int bn;               /* row stride of a partial slot (floats) */
-  int ld;
-  float lr;             /* learning rate x gradient scale */
-  int pad;
-} pkt_dp_reduce_args;
-
 typedef struct pkt_dp_bias_args {
   const float* partials; /* SEND: [num_partials, ld] column partial sums */
   float* bias;           /* APPLY: [n] updated in place */
@@ -162,8 +148,11 @@ enum pkt_epilogue {
   PKT_EPI_DGRAD_RELU = 3, /* out = acc * (aux > 0) */
   PKT_EPI_WGRAD_SGD = 4,  /* w_out = w_in - lr*acc (fp32), w_bf16 = bf16(w_out) */
   PKT_EPI_WGRAD_STORE = 5, /* out = acc (fp32 gradient) */
-  PKT_EPI_WGRAD_PEER = 6   /* fp32 partial tile into its owner rank's exchange region
-                              (MLP grad_mode 2 only) */
+  PKT_EPI_WGRAD_PEER = 6   /* fused data parallel (MLP grad_mode 2 only): a rank that
+                              does not own the tile sends its fp32 partial to the
+                              owner's exchange region; the owner sums the ranks'
+                              partials, applies SGD (w_in/w_out, lr) and writes the
+                              bf16 copy (w_shadow) on every rank */
 };
 
 /* One D[M,N] = sum_k A[m,k] B[n,k] problem, tiled 128 x bn. */

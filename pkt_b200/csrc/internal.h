@@ -102,9 +102,11 @@ struct alignas(128) DevGemm {
   int tma_out;     // 1: the epilogue writes `out` with TMA tile stores through map_out
   int tma_w;       // 1: WGRAD_SGD writes w_out / w_shadow through map_w / map_shadow
   int dp_tile_base;  // WGRAD_PEER: index of tile (0, 0) among all weight tiles of a step
+  int dp_layer;      // WGRAD_PEER: layer of the weights (counter of the next step's copies)
   CUtensorMap map_out;     // out: boxes of 32 columns x 32 rows (one compute warp's chunk)
   CUtensorMap map_w;       // w_out (fp32)
   CUtensorMap map_shadow;  // w_shadow (bf16)
+  CUtensorMap map_peer[PKT_DP_MAX_RANKS];  // WGRAD_PEER owner: w_shadow's twin on every rank
 };
 
 // Per-CTA perf words (pkt_runtime_fetch_perf), cycles unless noted.
@@ -134,13 +136,16 @@ struct DpPeers {
   int num_layers;
   long long slot_bytes;       // one partial tile slot: pair*128 rows x 256 floats
   long long recv_off;         // partial slots [owned tile][source rank]
-  long long arrive_off;       // int per owned tile: partial slots written (x pair)
+  long long arrive_off;       // int per owned tile: other ranks' partial slots written (x pair)
   long long wready_off;       // int per layer: owner broadcasts received (x pair)
   long long bias_recv_off;    // fp32 [2 step parities][world][bias_total]
   long long barrive_off;      // int per layer: bias vectors received (x pair)
   int bias_total;             // floats in one rank's bias gradient vector
   int pad_;
   uint8_t* base[PKT_DP_MAX_RANKS];
+  // per rank: its partial slots as one fp32 matrix [slots * pair*128 rows][256],
+  // boxes of 32 x 32 (TMA tile stores from a compute warp's staging buffer)
+  CUtensorMap recv_map[PKT_DP_MAX_RANKS];
 };
 
 struct KParams {

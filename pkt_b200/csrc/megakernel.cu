@@ -118,7 +118,7 @@ __device__ __forceinline__ bool opcode_known(uint16_t op) {
          op == PKT_OP_GEMM || op == PKT_OP_LINEAR_FORWARD || op == PKT_OP_MSE_LOSS ||
          op == PKT_OP_LINEAR_BACKWARD || op == PKT_OP_SGD_UPDATE || op == PKT_OP_BIAS_SGD ||
          op == PKT_OP_LOSS_REDUCE || op == PKT_OP_SGD_MIXED || op == PKT_OP_DP_WAIT ||
-         op == PKT_OP_DP_REDUCE || op == PKT_OP_DP_BIAS_SEND || op == PKT_OP_DP_BIAS_APPLY;
+         op == PKT_OP_DP_BIAS_SEND || op == PKT_OP_DP_BIAS_APPLY;
 }
 
 __device__ __forceinline__ void copy_task(pkt_task* dst, const pkt_task* src) {
@@ -621,6 +621,27 @@ __device__ __forceinline__ bool aligned16(const void* p) {
 }
 
 // ============================================================ GEMM epilogue
+// Waits (one thread) until *ctr >= target, reading at system scope: the
+// counter is advanced by other GPUs through peer memory. The budget is the
+// idle one: a peer may still be finishing its previous step.
+__device__ bool dp_wait_geq(const KParams& p, const int* ctr, int target, int where) {
+  if (ld_acquire_sys(ctr) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  const uint64_t budget = 4 * p.timeout_ns + 1000000000ull;
+  uint32_t it = 0;
+  while (ld_acquire_sys(ctr) < target) {
+    __nanosleep(64);
+    if ((++it & 15u) == 0) {
+      if (*status_word(p) != 0) return false;
+      if (globaltimer_ns() - t0 > budget) {
+        set_error(p, PKT_DEV_TIMEOUT_DEPS, -1, where);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
 template <int P>
 __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, const DevGemm& g,
                               int tile_m, int tile_n, uint32_t tmem_base, uint32_t acc,
@@ -662,22 +683,35 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
   const bool tma_out = g.tma_out != 0, tma_w = g.tma_w != 0;
   uint8_t* const stg = s.epi_stage[c.q];
   const int row0 = rblock * kBM + c.q * 32;
-  // WGRAD_PEER: this thread's row of the tile's partial slot in the owner
-  // rank's exchange region (slot rows are 256 floats apart).
-  float* peer_row = nullptr;
-  int* peer_arrive = nullptr;
-  if (epi == PKT_EPI_WGRAD_PEER) {
-    const DpPeers* dp = p.dp;
-    if (dp == nullptr) {
-      set_error(p, PKT_DEV_BAD_ARGS, -1, -3);
+  // WGRAD_PEER (fused data parallel): tile t belongs to rank t % world. A
+  // non-owner writes its fp32 partial rows into its slot in the owner's
+  // exchange region; the owner waits for the other ranks' slots, sums the
+  // partials in rank order (its own from TMEM), applies SGD to the master and
+  // writes the new bf16 rows into every rank's copy. Slot rows are 256 floats.
+  const DpPeers* dp = epi == PKT_EPI_WGRAD_PEER ? p.dp : nullptr;
+  if (epi == PKT_EPI_WGRAD_PEER && dp == nullptr) set_error(p, PKT_DEV_BAD_ARGS, -1, -3);
+  const int dp_t = g.dp_tile_base + tile_m * g.tiles_n + tile_n;
+  const bool dp_owner = dp != nullptr && dp_t % dp->world == dp->rank;
+  const int dp_tl = dp != nullptr ? dp_t / dp->world : 0;
+  const int slot_row = int(c.rank) * kBM + c.q * 32 + c.lane;
+  int peer_slot_row0 = 0;      // non-owner: the warp's first row in the owner's slot matrix
+  int* peer_arrive = nullptr;  // non-owner: the owner's arrival counter of this tile
+  const float* own_slots = nullptr;  // owner: slot 0 of this tile, this thread's row
+  long long shadow_off = 0;          // owner: byte offset of the bf16 copy in a region
+  if (dp != nullptr) {
+    const int owner = dp_t % dp->world;
+    uint8_t* ob = dp->base[owner];
+    const float* slots0 = reinterpret_cast<const float*>(ob + dp->recv_off + (long long)dp_tl * dp->world * dp->slot_bytes);
+    if (!dp_owner) {
+      peer_slot_row0 = int(((long long)dp_tl * dp->world + dp->rank) * dp->pair * kBM) + int(c.rank) * kBM + c.q * 32;
+      peer_arrive = reinterpret_cast<int*>(ob + dp->arrive_off) + dp_tl;
     } else {
-      const int t = g.dp_tile_base + tile_m * g.tiles_n + tile_n;
-      const int owner = t % dp->world, tl = t / dp->world;
-      uint8_t* ob = dp->base[owner];
-      peer_row = reinterpret_cast<float*>(ob + dp->recv_off +
-                                          ((long long)tl * dp->world + dp->rank) * dp->slot_bytes) +
-                 (long long)(int(c.rank) * kBM + c.q * 32 + c.lane) * 256;
-      peer_arrive = reinterpret_cast<int*>(ob + dp->arrive_off) + tl;
+      own_slots = slots0 + (long long)slot_row * 256;
+      shadow_off = reinterpret_cast<const uint8_t*>(w_shadow) - dp->base[dp->rank];
+      if (c.et == 0 && dp->world > 1)
+        dp_wait_geq(p, reinterpret_cast<const int*>(ob + dp->arrive_off) + dp_tl,
+                    (p.dp_step + 1) * (dp->world - 1) * dp->pair, 4000 + g.dp_layer);
+      epi_sync();
     }
   }
   auto emit_out = [&](float (&vv)[32], int col0, int nvalid) {
@@ -778,13 +812,44 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = (j < nvalid && h[j] > 0.f) ? v[j] : 0.f;
       emit_out(v, col0, nvalid);
-    } else if (epi == PKT_EPI_WGRAD_PEER) {
-      if (peer_row != nullptr) {
-        float4* dst = reinterpret_cast<float4*>(peer_row + ch * 32);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else if (epi == PKT_EPI_WGRAD_PEER && !dp_owner) {
+      // the warp's 32 x 32 fp32 chunk goes to the owner as one TMA tile store
+      if (dp != nullptr) {
+        if (c.lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        stage_row32(stg, PKT_DTYPE_F32, c.lane, v);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (c.lane == 0) {
+          tma_store_2d(&dp->recv_map[dp_t % dp->world], stg, ch * 32, peer_slot_row0);
+          bulk_commit();
+        }
       }
-    } else if (epi == PKT_EPI_WGRAD_SGD) {
+    } else if (epi == PKT_EPI_WGRAD_SGD || dp_owner) {
+      if (dp_owner) {
+        // rank-ordered sum of the partials; this rank's own is v
+        float gsum[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) gsum[j] = 0.f;
+        for (int src = 0; src < dp->world; ++src) {
+          if (src == dp->rank) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) gsum[j] += v[j];
+          } else {
+            const float4* pr = reinterpret_cast<const float4*>(own_slots + src * (dp->slot_bytes / 4) + ch * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 q4 = __ldcg(pr + i);
+              gsum[4 * i] += q4.x;
+              gsum[4 * i + 1] += q4.y;
+              gsum[4 * i + 2] += q4.z;
+              gsum[4 * i + 3] += q4.w;
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gsum[j];
+      }
       float w[32];
       const long long ow = (long long)row * ldw + col0;
       const bool wvec = aligned16(w_in + ow) && aligned16(w_out + ow);
@@ -806,6 +871,9 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
         if (c.lane == 0 && row0 < M && col0 < N) {
           tma_store_2d(&g.map_w, stg, col0, row0);
           if (w_shadow) tma_store_2d(&g.map_shadow, stg + 4096, col0, row0);
+          if (dp_owner)  // the new bf16 chunk into the other ranks' copies
+            for (int r2 = 0; r2 < dp->world; ++r2)
+              if (r2 != dp->rank) tma_store_2d(&g.map_peer[r2], stg + 4096, col0, row0);
           bulk_commit();
         }
       } else if (nvalid > 0) {
@@ -819,6 +887,25 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
         if (w_shadow) {
           const bool svec = aligned16(reinterpret_cast<const uint16_t*>(w_shadow) + ow);
           store_row32(w_shadow, PKT_DTYPE_BF16, ow, nvalid, svec, w2);
+        }
+      }
+      if (dp_owner && !tma_w && nvalid > 0) {
+        // the new bf16 row into the other ranks' copies (w holds the new master,
+        // possibly already rounded to bf16: rounding again changes nothing)
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(w[2 * i], w[2 * i + 1]);
+        for (int r2 = 0; r2 < dp->world; ++r2) {
+          if (r2 == dp->rank) continue;
+          uint16_t* dst = reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + ow;
+          if (nvalid == 32 && aligned16(dst)) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          } else {
+            for (int j = 0; j < nvalid; ++j)
+              dst[j] = uint16_t((j & 1) ? (pk[j >> 1] >> 16) : (pk[j >> 1] & 0xffffu));
+          }
         }
       }
     }
@@ -864,14 +951,22 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
   }
   // The tile's TMA stores have landed in global memory before the caller
   // publishes the tile's completion.
-  if ((tma_out || tma_w) && c.lane == 0) bulk_wait_all();
+  if ((tma_out || tma_w || dp != nullptr) && c.lane == 0) bulk_wait_all();
   __syncwarp();
-  if (epi == PKT_EPI_WGRAD_PEER) {
-    // every thread's partial rows visible system-wide, then one arrive per CTA
-    // on the owner's counter for this tile
+  if (dp != nullptr) {
+    // every thread's rows (TMA stores included) visible system-wide, then one
+    // arrive per CTA: a non-owner on the owner's counter of this tile, the
+    // owner on every rank's counter of the layer's next-step weights
+    fence_proxy_async_global();
     __threadfence_system();
     epi_sync();
-    if (c.et == 0 && peer_arrive != nullptr) red_release_sys_add(peer_arrive, 1);
+    if (c.et == 0) {
+      if (!dp_owner)
+        red_release_sys_add(peer_arrive, 1);
+      else
+        for (int r2 = 0; r2 < dp->world; ++r2)
+          red_release_sys_add(reinterpret_cast<int*>(dp->base[r2] + dp->wready_off) + g.dp_layer, 1);
+    }
   }
 }
 
@@ -1047,27 +1142,6 @@ __device__ void op_bias_sgd(const pkt_bias_sgd_args& a, int et, int nthr) {
 }
 
 // ============================================================ fused data parallel
-// Waits (one thread) until *ctr >= target, reading at system scope: the
-// counter is advanced by other GPUs through peer memory. The budget is the
-// idle one: a peer may still be finishing its previous step.
-__device__ bool dp_wait_geq(const KParams& p, const int* ctr, int target, int where) {
-  if (ld_acquire_sys(ctr) >= target) return true;
-  const uint64_t t0 = globaltimer_ns();
-  const uint64_t budget = 4 * p.timeout_ns + 1000000000ull;
-  uint32_t it = 0;
-  while (ld_acquire_sys(ctr) < target) {
-    __nanosleep(64);
-    if ((++it & 15u) == 0) {
-      if (*status_word(p) != 0) return false;
-      if (globaltimer_ns() - t0 > budget) {
-        set_error(p, PKT_DEV_TIMEOUT_DEPS, -1, where);
-        return false;
-      }
-    }
-  }
-  return true;
-}
-
 // Next step's weights of one layer: every owner's broadcast of every tile of
 // the layer (one arrive per CTA of the owner's pair) has landed here.
 __device__ void op_dp_wait(const KParams& p, const EpiCtx& c, const pkt_dp_wait_args& a) {
@@ -1077,65 +1151,6 @@ __device__ void op_dp_wait(const KParams& p, const EpiCtx& c, const pkt_dp_wait_
     dp_wait_geq(p, ctr, p.dp_step * a.tiles * dp->pair, 1000 + a.layer);
   }
   epi_sync();
-}
-
-// Owner side of one weight tile: sum the ranks' fp32 partials in rank order,
-// fp32 master -= lr * sum, and write bf16(master) into every rank's copy for the
-// next step; then one arrive per CTA on every rank's layer counter.
-__device__ void op_dp_reduce(const KParams& p, const EpiCtx& c, const pkt_dp_reduce_args& a) {
-  const DpPeers* dp = p.dp;
-  if (dp == nullptr) return;
-  uint8_t* own = dp->base[dp->rank];
-  if (c.et == 0) {
-    const int* ctr = reinterpret_cast<const int*>(own + dp->arrive_off) + a.tile_local;
-    dp_wait_geq(p, ctr, (p.dp_step + 1) * dp->world * dp->pair, 2000 + a.layer);
-  }
-  epi_sync();
-  const long long sfl = dp->slot_bytes / 4;  // floats per slot
-  const float* slots = reinterpret_cast<const float*>(own + dp->recv_off) + (long long)a.tile_local * dp->world * sfl;
-  float* master = reinterpret_cast<float*>(own + a.master_off) + a.w_elem;
-  const int cq = (a.cols + 3) / 4;
-  const int world = dp->world;
-  for (int idx = c.tid; idx < a.rows * cq; idx += c.nthr) {
-    const int r = idx / cq, c4 = (idx - r * cq) * 4;
-    const long long so = (long long)r * a.bn + c4;
-    float* m = master + (long long)r * a.ld + c4;
-    const long long we = a.w_elem + (long long)r * a.ld + c4;
-    if (c4 + 4 <= a.cols) {
-      float4 gs = __ldcg(reinterpret_cast<const float4*>(slots + so));
-      for (int src = 1; src < world; ++src) {
-        const float4 q = __ldcg(reinterpret_cast<const float4*>(slots + src * sfl + so));
-        gs.x += q.x;
-        gs.y += q.y;
-        gs.z += q.z;
-        gs.w += q.w;
-      }
-      float4 w = *reinterpret_cast<float4*>(m);
-      w.x = fmaf(-a.lr, gs.x, w.x);
-      w.y = fmaf(-a.lr, gs.y, w.y);
-      w.z = fmaf(-a.lr, gs.z, w.z);
-      w.w = fmaf(-a.lr, gs.w, w.w);
-      *reinterpret_cast<float4*>(m) = w;
-      const uint2 b = make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
-      for (int r2 = 0; r2 < world; ++r2)
-        *reinterpret_cast<uint2*>(dp->base[r2] + a.wbf_off + we * 2) = b;
-    } else {
-      for (int j = 0; j < a.cols - c4; ++j) {
-        float gs = __ldcg(slots + so + j);
-        for (int src = 1; src < world; ++src) gs += __ldcg(slots + src * sfl + so + j);
-        const float w = fmaf(-a.lr, gs, m[j]);
-        m[j] = w;
-        const uint16_t h = uint16_t(pack_bf16x2(w, 0.f) & 0xffffu);
-        for (int r2 = 0; r2 < world; ++r2)
-          *reinterpret_cast<uint16_t*>(dp->base[r2] + a.wbf_off + (we + j) * 2) = h;
-      }
-    }
-  }
-  __threadfence_system();
-  epi_sync();
-  if (c.et == 0)
-    for (int r2 = 0; r2 < world; ++r2)
-      red_release_sys_add(reinterpret_cast<int*>(dp->base[r2] + dp->wready_off) + a.layer, 1);
 }
 
 // This rank's bias gradient of one layer (column partials summed in row-block
@@ -1254,9 +1269,6 @@ __device__ void compute_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base, 
         break;
       case PKT_OP_DP_WAIT:
         op_dp_wait(p, c, *reinterpret_cast<const pkt_dp_wait_args*>(task.args));
-        break;
-      case PKT_OP_DP_REDUCE:
-        op_dp_reduce(p, c, *reinterpret_cast<const pkt_dp_reduce_args*>(task.args));
         break;
       case PKT_OP_DP_BIAS_SEND:
         op_dp_bias_send(p, c, *reinterpret_cast<const pkt_dp_bias_args*>(task.args));

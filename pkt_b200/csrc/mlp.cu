@@ -356,6 +356,11 @@ int Mlp::connect(int rank, int world, const uint8_t* handles) {
   }
   hdp.world = world;
   hdp.rank = rank;
+  const long long slot_rows = (long long)P * kBM, nslots = wg_total + PKT_DP_MAX_RANKS;
+  for (int r = 0; r < world; ++r)
+    if (!make_store_map(&hdp.recv_map[r], hdp.base[r] + hdp.recv_off, PKT_DTYPE_F32, 256,
+                        nslots * slot_rows, 256))
+      return fail(PKT_ERR_CUDA, "tensor map over rank %d's partial slots", r);
   cudaError_t e = cudaMalloc(&d_dp, sizeof(DpPeers));
   if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(peer table)");
   e = cudaMemcpy(d_dp, &hdp, sizeof(DpPeers), cudaMemcpyHostToDevice);
@@ -450,7 +455,14 @@ int Mlp::build(int p, int q) {
     d.b_major = PKT_MAJOR_MN;
     d.bn = pick_bn(d.M, d.N, true);
     if (grad_mode == 2) {
+      // the owner of a tile applies SGD to its master shard and writes the bf16
+      // copy the next step reads (locally here, on the other ranks in the kernel)
       d.epilogue = PKT_EPI_WGRAD_PEER;
+      d.w_in = Wmaster(l, cur);
+      d.w_out = Wmaster(l, nxt);
+      d.w_shadow = Wbf[nxt][l];
+      d.ldw = ld[l];
+      d.lr = lr * grad_scale;
       d.out = nullptr;
     } else if (grad_mode == 0) {
       d.epilogue = PKT_EPI_WGRAD_SGD;
@@ -481,6 +493,11 @@ int Mlp::build(int p, int q) {
       if (dg.tiles_m != wg_tm[l] || dg.tiles_n != wg_tn[l] || dg.d.bn != wg_bn[l])
         return fail(PKT_ERR_UNSUPPORTED, "weight tile layout differs from the exchange region's");
       dg.dp_tile_base = wg_base[l];
+      dg.dp_layer = l;
+      for (int r = 0; r < dp_world; ++r)
+        if (!make_store_map(&dg.map_peer[r], hdp.base[r] + wbf_off[nxt][l], PKT_DTYPE_BF16, dims[l],
+                            dims[l + 1], ld[l]))
+          return fail(PKT_ERR_CUDA, "tensor map over rank %d's weight copy", r);
       cudaError_t e = cudaMemcpy(rt->d_gemms + first + wgr[l], &dg, sizeof(DevGemm), cudaMemcpyHostToDevice);
       if (e != cudaSuccess) return cuda_fail(e, "copy gemm table");
     }
@@ -616,35 +633,9 @@ int Mlp::build(int p, int q) {
     }
   } else {
     // Fused data parallel: each layer's weight-gradient tiles follow its dgrad
-    // tiles, so partial tiles start crossing to their owners early in the
-    // backward; the owner's reduce tasks of layer l+1 come after the tiles of
-    // layer l (by then every rank has usually sent its partials).
+    // tiles, so partial tiles cross to their owners (and the owners' new
+    // weights back) while the rest of the backward runs.
     const float lre = lr * grad_scale;
-    const int world = dp_world > 0 ? dp_world : 1, me = dp_world > 0 ? dp_rank : 0;
-    auto reduce_tasks = [&](int l) {
-      const int M = dims[l + 1], N = dims[l], rows_t = kBM * P;
-      for (int i = 0; i < wg_tm[l]; ++i)
-        for (int j = 0; j < wg_tn[l]; ++j) {
-          const int t = wg_base[l] + i * wg_tn[l] + j;
-          if (t % world != me) continue;
-          pkt_task tk{};
-          tk.header.opcode = PKT_OP_DP_REDUCE;
-          pkt_dp_reduce_args a{};
-          a.master_off = master_off[l];
-          a.wbf_off = wbf_off[nxt][l];
-          a.w_elem = (long long)i * rows_t * ld[l] + (long long)j * wg_bn[l];
-          a.layer = l;
-          a.tile_local = t / world;
-          a.rows = std::min(rows_t, M - i * rows_t);
-          a.cols = std::min(wg_bn[l], N - j * wg_bn[l]);
-          a.bn = 256;
-          a.ld = ld[l];
-          a.lr = lre;
-          tk.header.arg_bytes = sizeof(a);
-          std::memcpy(tk.args, &a, sizeof(a));
-          tl.push_back(tk);
-        }
-    };
     for (int l = L - 1; l >= 0; --l) {
       if (l >= 1) {
         const DevGemm& dg = G(dgr[l]);
@@ -659,15 +650,24 @@ int Mlp::build(int p, int q) {
             ++tiles;
           }
       }
+      // Tiles grouped by owner rank, this rank's own group last: every other
+      // rank visits this rank's group earlier in its own order, so when an
+      // owner reaches its tiles the other ranks' partials are normally there
+      // (and every wait points at a tile earlier in the peer's list).
       const DevGemm& wg = G(wgr[l]);
-      for (int i = 0; i < wg.tiles_m; ++i)
-        for (int j = 0; j < wg.tiles_n; ++j) {
-          pkt_task t = gemm_task(wgr[l], i, j);
-          t.header.buffer_read_id = uint16_t(BF[l]);
-          t.header.wait_count = uint32_t(TM * dy_tn[l]);
-          tl.push_back(t);
-          ++tiles;
-        }
+      const int world = dp_world > 0 ? dp_world : 1, me = dp_world > 0 ? dp_rank : 0;
+      for (int k = 1; k <= world; ++k) {
+        const int owner = (me + k) % world;
+        for (int i = 0; i < wg.tiles_m; ++i)
+          for (int j = 0; j < wg.tiles_n; ++j) {
+            if ((wg_base[l] + i * wg.tiles_n + j) % world != owner) continue;
+            pkt_task t = gemm_task(wgr[l], i, j);
+            t.header.buffer_read_id = uint16_t(BF[l]);
+            t.header.wait_count = uint32_t(TM * dy_tn[l]);
+            tl.push_back(t);
+            ++tiles;
+          }
+      }
       if (has_bias) {
         pkt_task t{};
         t.header.opcode = PKT_OP_DP_BIAS_SEND;
@@ -684,9 +684,7 @@ int Mlp::build(int p, int q) {
         t.header.wait_count = uint32_t(TM * dy_tn[l]);
         tl.push_back(t);
       }
-      if (l + 1 < L) reduce_tasks(l + 1);
     }
-    reduce_tasks(0);
     if (has_bias) {
       for (int l = L - 1; l >= 0; --l) {
         pkt_task t{};

@@ -87,7 +87,7 @@ static int make_map(CUtensorMap* map, const void* base, int dtype, long long col
 // rows for fp32) so the warp's row-per-lane shared-memory writes are free of
 // bank conflicts. Returns false (and the epilogue keeps its plain stores) where
 // TMA cannot address the matrix.
-static bool make_store_map(CUtensorMap* map, const void* base, int dtype, long long cols,
+bool make_store_map(CUtensorMap* map, const void* base, int dtype, long long cols,
                            long long rows, long long ld) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc || base == nullptr) return false;
@@ -194,13 +194,13 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
   if (!d.out && d.epilogue != PKT_EPI_WGRAD_SGD && d.epilogue != PKT_EPI_WGRAD_PEER) return fail(PKT_ERR_ARGS, "GEMM output pointer missing");
   if ((d.epilogue == PKT_EPI_MSE || d.epilogue == PKT_EPI_DGRAD_RELU) && !d.aux)
     return fail(PKT_ERR_ARGS, "MSE / DGRAD epilogue needs aux");
-  if (d.epilogue == PKT_EPI_WGRAD_SGD && (!d.w_in || !d.w_out))
-    return fail(PKT_ERR_ARGS, "WGRAD_SGD epilogue needs w_in / w_out");
+  if ((d.epilogue == PKT_EPI_WGRAD_SGD || d.epilogue == PKT_EPI_WGRAD_PEER) && (!d.w_in || !d.w_out))
+    return fail(PKT_ERR_ARGS, "WGRAD_SGD / WGRAD_PEER epilogues need w_in / w_out");
   if (d.epilogue < 0 || d.epilogue > PKT_EPI_WGRAD_PEER) return fail(PKT_ERR_ARGS, "bad epilogue");
   // TMA tile stores need whole 32-column chunks inside a tile (a box must not
   // spill into the neighbouring tile's columns).
   if (d.bn % 32 == 0) {
-    if (d.epilogue == PKT_EPI_WGRAD_SGD) {
+    if (d.epilogue == PKT_EPI_WGRAD_SGD || d.epilogue == PKT_EPI_WGRAD_PEER) {
       g->tma_w = make_store_map(&g->map_w, d.w_out, PKT_DTYPE_F32, d.N, d.M, d.ldw) &&
                  (d.w_shadow == nullptr ||
                   make_store_map(&g->map_shadow, d.w_shadow, PKT_DTYPE_BF16, d.N, d.M, d.ldw));

@@ -13,6 +13,8 @@ int fail(int code, const char* fmt, ...);
 int cuda_fail(cudaError_t e, const char* what);
 int gemm_tiles(const pkt_gemm_desc& d, int* tm, int* tn);
 int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g);
+bool make_store_map(CUtensorMap* map, const void* base, int dtype, long long cols, long long rows,
+                    long long ld);
 
 struct Runtime {
   int device = -1;
