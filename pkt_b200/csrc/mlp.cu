@@ -636,6 +636,7 @@ int Mlp::build(int p, int q) {
     // tiles, so partial tiles cross to their owners (and the owners' new
     // weights back) while the rest of the backward runs.
     const float lre = lr * grad_scale;
+    std::vector<pkt_task> deferred;  // this rank's own weight tiles of the previous layer
     for (int l = L - 1; l >= 0; --l) {
       if (l >= 1) {
         const DevGemm& dg = G(dgr[l]);
@@ -648,14 +649,26 @@ int Mlp::build(int p, int q) {
             t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
             tl.push_back(t);
             ++tiles;
+            // this rank's own weight tiles of layer l+1 go in after two waves of
+            // these dgrad tiles
+            if (!deferred.empty() && (i * dg.tiles_n + j + 1) == 2 * std::max(1, rt->num_sms / P)) {
+              for (auto& d2 : deferred) tl.push_back(d2);
+              deferred.clear();
+            }
           }
+        for (auto& d2 : deferred) tl.push_back(d2);
+        deferred.clear();
       }
-      // Tiles grouped by owner rank, this rank's own group last: every other
-      // rank visits this rank's group earlier in its own order, so when an
-      // owner reaches its tiles the other ranks' partials are normally there
-      // (and every wait points at a tile earlier in the peer's list).
+      if (l == 0) { for (auto& d2 : deferred) tl.push_back(d2); deferred.clear(); }
+      // Tiles grouped by owner rank; this rank's own group (whose epilogues wait
+      // for the other ranks' partials) is deferred into the next layer's dgrad
+      // block (wgrad(0)'s stays last): every other rank visits that group
+      // earlier in its own order, so the partials have normally arrived when
+      // the owner gets there, and every wait points at a tile earlier in the
+      // peer's list.
       const DevGemm& wg = G(wgr[l]);
       const int world = dp_world > 0 ? dp_world : 1, me = dp_world > 0 ? dp_rank : 0;
+      std::vector<pkt_task> own_now;
       for (int k = 1; k <= world; ++k) {
         const int owner = (me + k) % world;
         for (int i = 0; i < wg.tiles_m; ++i)
@@ -664,7 +677,7 @@ int Mlp::build(int p, int q) {
             pkt_task t = gemm_task(wgr[l], i, j);
             t.header.buffer_read_id = uint16_t(BF[l]);
             t.header.wait_count = uint32_t(TM * dy_tn[l]);
-            tl.push_back(t);
+            if (owner == me && l >= 1 && world > 1) deferred.push_back(t); else tl.push_back(t);
             ++tiles;
           }
       }
