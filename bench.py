@@ -1,4 +1,4 @@
-"""Benchmark of the pkt MLP training step on B200 (see DESIGN.md for the method).
+"""Benchmark of the pkt MLP training step on B200.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg2]
 
