@@ -224,10 +224,43 @@ def run_ours(args, cfg_name, cfg):
     from pkt_b200.mlp import to_bf16_bits
 
     dims, B = cfg["dims"], cfg["batch"]
-    nccl_dp = ws > 1 and args.dp == "nccl"
-    grad_mode = (1 if nccl_dp else 2) if ws > 1 else 0
-    eng = pkt_b200.MLP(dims, B, dtype=cfg["dtype"], lr=cfg["lr"], bias=True, grad_mode=grad_mode,
-                       device=local)
+    # fused data parallel needs bf16 weights; TF32 configs use the NCCL path
+    nccl_dp = ws > 1 and (args.dp == "nccl" or cfg["dtype"] != "bf16")
+
+    def make_engine(gm):
+        return pkt_b200.MLP(dims, B, dtype=cfg["dtype"], lr=cfg["lr"], bias=True, grad_mode=gm,
+                            device=local)
+
+    eng = make_engine((1 if nccl_dp else 2) if ws > 1 else 0)
+    if ws > 1 and not nccl_dp:
+        # exchange the ranks' peer-memory handles once; if any rank cannot map its
+        # peers, every rank falls back to the NCCL all-reduce path together
+        ok, handle = 1, b""
+        try:
+            handle = eng.dp_handle()
+        except Exception as e:  # noqa: BLE001
+            print(f"rank {rank}: no exchange-region handle ({e})", file=sys.stderr)
+            ok = 0
+        handles = [None] * ws
+        dist.all_gather_object(handles, (ok, handle))
+        if all(h[0] for h in handles):
+            try:
+                eng.dp_connect(rank, ws, [h[1] for h in handles])
+            except Exception as e:  # noqa: BLE001
+                print(f"rank {rank}: cannot map the peers' exchange regions ({e})", file=sys.stderr)
+                ok = 0
+        else:
+            ok = 0
+        flag = torch.tensor([ok], device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        torch.cuda.synchronize()
+        dist.barrier()
+        if int(flag.item()) == 0:
+            if rank == 0:
+                print("fused data parallel unavailable: using the NCCL all-reduce path", file=sys.stderr)
+            eng.close()
+            nccl_dp = True
+            eng = make_engine(1)
     if ws > 1:
         eng.set_grad_scale(1.0 / ws)
     x, t, Ws, bs = make_inputs(cfg, 0)  # same initial weights on every rank
@@ -251,13 +284,6 @@ def run_ours(args, cfg_name, cfg):
     if nccl_dp:
         gptr, gcount = eng.grad_buffer()
         grad_t = _wrap_device_f32(gptr, gcount, local)
-    elif ws > 1:
-        # fused data parallel: exchange the ranks' peer-memory handles once
-        handles = [None] * ws
-        dist.all_gather_object(handles, eng.dp_handle())
-        eng.dp_connect(rank, ws, handles)
-        torch.cuda.synchronize()
-        dist.barrier()
 
     def step(s_ptr):
         if nccl_dp:
