@@ -2,6 +2,7 @@
 
     python -m pkt_b200.perf_report --dims 1024,4096,4096,4096,1024 --batch 8192
     python -m torch.distributed.run --nproc-per-node 8 -m pkt_b200.perf_report --grad-mode 2
+    python -m pkt_b200.perf_report --axpy 268435456
 
 Times `--steps` steps with CUDA events, then runs one more step with the
 per-CTA counters on and prints, for the leader CTA of every CTA pair, the mean
@@ -13,6 +14,9 @@ the engine runs data parallel: grad_mode 2 (default there) reduces the weight
 gradients inside the step over peer memory, grad_mode 1 with an NCCL all-reduce
 between the backward and the update launch; every rank prints its step time and
 rank 0 its counters.
+
+--axpy N instead times pkt_axpy (y = a*x + y over N floats already on the device,
+12 bytes per element: read x, read y, write y) and prints its HBM bandwidth.
 """
 import argparse
 import os
@@ -31,6 +35,29 @@ def _wrap_f32(ptr, count, device):
     return torch.as_tensor(_CAI(), device=torch.device("cuda", device))
 
 
+def axpy_report(args):
+    import torch
+    import pkt_b200
+
+    n = args.axpy
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    x = torch.rand(n, device="cuda")
+    y = torch.rand(n, device="cuda")
+    for _ in range(args.warmup):
+        pkt_b200.axpy(x.data_ptr(), y.data_ptr(), 0.5, n)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    ev[0].record()
+    for i in range(args.steps):
+        pkt_b200.axpy(x.data_ptr(), y.data_ptr(), 0.5, n)
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    per = sorted(ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps))
+    ms = per[len(per) // 2]
+    print(f"axpy n={n}: {ms:.3f} ms per call (median of {args.steps}), "
+          f"{12.0 * n / ms / 1e6:.0f} GB/s (12 B per element)")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--dims", default="1024,4096,4096,4096,1024")
@@ -41,7 +68,11 @@ def main(argv=None):
     ap.add_argument("--grad-mode", type=int, default=None, choices=[0, 1, 2],
                     help="0: SGD fused into the gradient epilogue (one GPU); 1: NCCL all-reduce; "
                          "2: fused peer-memory reduce (default with WORLD_SIZE > 1)")
+    ap.add_argument("--axpy", type=int, default=0, metavar="N",
+                    help="time pkt_axpy over N floats instead of an MLP step")
     args = ap.parse_args(argv)
+    if args.axpy:
+        return axpy_report(args)
 
     import torch
     import pkt_b200
