@@ -597,15 +597,18 @@ int Mlp::build(int p, int q) {
     }
     for (int l = L - 1; l >= 0; --l) {
       const DevGemm& wg = G(wgr[l]);
-      for (int i = 0; i < wg.tiles_m; ++i)
-        for (int j = 0; j < wg.tiles_n; ++j) {
-          pkt_task t = gemm_task(wgr[l], i, j);
-          t.header.buffer_read_id = uint16_t(BF[l]);
-          t.header.wait_count = uint32_t(TM * dy_tn[l]);
-          t.header.buffer_write_id = uint16_t(WG_base + l);
-          tl.push_back(t);
-          ++tiles;
-        }
+      // groups of 8 tile rows swept column by column: the tiles in flight share
+      // fewer operand blocks, so more of them stay in L2
+      for (int i0 = 0; i0 < wg.tiles_m; i0 += 8)
+        for (int j = 0; j < wg.tiles_n; ++j)
+          for (int i = i0; i < std::min(wg.tiles_m, i0 + 8); ++i) {
+            pkt_task t = gemm_task(wgr[l], i, j);
+            t.header.buffer_read_id = uint16_t(BF[l]);
+            t.header.wait_count = uint32_t(TM * dy_tn[l]);
+            t.header.buffer_write_id = uint16_t(WG_base + l);
+            tl.push_back(t);
+            ++tiles;
+          }
       if (has_bias) {
         const int n = dims[l + 1];
         for (int c0 = 0; c0 < n; c0 += 512) {
