@@ -217,7 +217,8 @@ int pkt_gemm_tiles(const pkt_gemm_desc* d, int* tiles_m, int* tiles_n);
 /* Wait budget of every device-side spin, in nanoseconds (default 2e9). */
 int pkt_runtime_set_timeout_ns(pkt_runtime* rt, unsigned long long ns);
 /* Launch mode: 1 = one CTA per SM works alone (default); 2 = CTA pairs (clusters of
- * two SMs) share 256-row GEMM tiles; the block count is rounded up to even. */
+ * two SMs) share 256-row GEMM tiles. pkt_runtime_launch clamps the grid to the CTAs
+ * that can be resident at once and, in pair mode, rounds it to whole clusters. */
 int pkt_runtime_set_cta_pair(pkt_runtime* rt, int pair);
 int pkt_runtime_set_task_accounting(pkt_runtime* rt, int enabled);
 int pkt_runtime_fetch_task_counter(pkt_runtime* rt, unsigned long long* out);
@@ -226,6 +227,11 @@ int pkt_runtime_set_perf(pkt_runtime* rt, int enabled);
 #define PKT_PERF_WORDS 16
 int pkt_runtime_fetch_perf(pkt_runtime* rt, unsigned long long* out, int max_blocks, int* blocks);
 int pkt_runtime_last_launch_blocks(pkt_runtime* rt);
+/* Effective SM clock of the launches since the last reset (no counterpart in pkt):
+ * out3 = {SM cycles, nanoseconds, launches} summed over CTA 0's lifetime in every
+ * launch; cycles * 1000 / ns is the mean SM clock in MHz. reset != 0 clears the
+ * sums after reading them (out3 may be NULL to clear only). */
+int pkt_runtime_clock_stats(pkt_runtime* rt, unsigned long long* out3, int reset);
 int pkt_num_sms(int device);
 const char* pkt_last_error(void);
 
@@ -240,6 +246,14 @@ int pkt_axpy(const float* x, float* y, float a, long long n, void* stream);
  * order them on one stream. The first call on a device looks up the array's
  * address and should come before any stream capture. */
 int pkt_axpy_noalloc(const float* x, float* y, float a, long long n, void* stream);
+/* Device status words of the last pkt_axpy_noalloc launch on the current device
+ * (code PKT_DEV_*, task index, detail; all 0 when it ran cleanly), read from the
+ * same fixed array without allocating. Synchronises the device first, so call it
+ * after the work to check, not inside a stream capture. Every wait in that launch
+ * has a fixed budget of 2 s; a launch that ran out of it reports
+ * PKT_DEV_TIMEOUT_PIPE or PKT_DEV_TIMEOUT_DEPS here. The next pkt_axpy_noalloc
+ * call clears the words. */
+int pkt_axpy_noalloc_status(int* code, int* task_index, int* detail);
 
 /* ---- MLP training engine (the hot path) -------------------------------- */
 typedef struct pkt_mlp pkt_mlp;
@@ -315,6 +329,8 @@ int pkt_mlp_dp_connect(pkt_mlp* m, int rank, int world, const void* handles);
 /* Per-CTA role cycle counters of the last launch (same layout as pkt_runtime_fetch_perf). */
 int pkt_mlp_set_perf(pkt_mlp* m, int enabled);
 int pkt_mlp_fetch_perf(pkt_mlp* m, unsigned long long* out, int max_blocks, int* blocks);
+/* Effective SM clock of the engine's launches, as pkt_runtime_clock_stats. */
+int pkt_mlp_clock_stats(pkt_mlp* m, unsigned long long* out3, int reset);
 
 #ifdef __cplusplus
 }

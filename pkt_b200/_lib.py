@@ -82,8 +82,10 @@ _SIGS = {
     "pkt_runtime_set_perf": ([_P, c_int], c_int),
     "pkt_runtime_fetch_perf": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
     "pkt_runtime_last_launch_blocks": ([_P], c_int),
+    "pkt_runtime_clock_stats": ([_P, _P, c_int], c_int),
     "pkt_axpy": ([_P, _P, c_float, c_longlong, _P], c_int),
     "pkt_axpy_noalloc": ([_P, _P, c_float, c_longlong, _P], c_int),
+    "pkt_axpy_noalloc_status": ([_P, _P, _P], c_int),
     "pkt_mlp_create": ([c_int, _P, ctypes.POINTER(_P)], c_int),
     "pkt_mlp_destroy": ([_P], c_int),
     "pkt_mlp_set_params": ([_P, _P, _P], c_int),
@@ -106,6 +108,7 @@ _SIGS = {
     "pkt_mlp_apply_update": ([_P, _P], c_int),
     "pkt_mlp_set_perf": ([_P, c_int], c_int),
     "pkt_mlp_fetch_perf": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
+    "pkt_mlp_clock_stats": ([_P, _P, c_int], c_int),
 }
 
 EXPORTS = sorted(_SIGS)

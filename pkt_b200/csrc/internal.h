@@ -161,12 +161,18 @@ struct KParams {
   unsigned long long timeout_ns;
   const DpPeers* dp;  // fused data parallel (null otherwise)
   int dp_step;        // fused data-parallel steps completed before this launch
+  // optional [3]: += SM cycles, += nanoseconds of CTA 0's lifetime, += 1 per launch
+  unsigned long long* clock_acc;
 };
 
 constexpr int kStateHeader = 8;  // ints before the token counters
 inline int state_ints(int num_tokens) { return kStateHeader + 2 * num_tokens; }
 
 // Launches the megakernel (megakernel.cu); pair = 2 launches clusters of two CTAs.
+// `blocks` must not exceed max_resident_blocks(pair): every CTA of the persistent
+// grid is resident at once.
 cudaError_t launch_megakernel(const KParams& p, int blocks, cudaStream_t stream, int pair = 1);
+// CTAs of the megakernel variant that fit on the current device at the same time.
+cudaError_t max_resident_blocks(int pair, int* blocks);
 
 }  // namespace pkb

@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -52,7 +53,7 @@ struct SmemT {
   uint64_t mma_drain;
   uint64_t pair_done[kSlots];  // leader: the other CTA of the pair finished task seq
   uint32_t tmem_base;
-  uint32_t pad0;
+  int dp_ok;  // WGRAD_PEER owner: the other ranks' partials of the current tile arrived
   float red[8][4][32];  // per 32-column chunk, per TMEM lane quadrant: column partial sums
   float lossred[4];
   float simt_red[4];
@@ -698,6 +699,7 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
   int* peer_arrive = nullptr;  // non-owner: the owner's arrival counter of this tile
   const float* own_slots = nullptr;  // owner: slot 0 of this tile, this thread's row
   long long shadow_off = 0;          // owner: byte offset of the bf16 copy in a region
+  bool dp_skip = false;              // owner whose wait for the partials failed
   if (dp != nullptr) {
     const int owner = dp_t % dp->world;
     uint8_t* ob = dp->base[owner];
@@ -708,10 +710,17 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
     } else {
       own_slots = slots0 + (long long)slot_row * 256;
       shadow_off = reinterpret_cast<const uint8_t*>(w_shadow) - dp->base[dp->rank];
-      if (c.et == 0 && dp->world > 1)
-        dp_wait_geq(p, reinterpret_cast<const int*>(ob + dp->arrive_off) + dp_tl,
-                    (p.dp_step + 1) * (dp->world - 1) * dp->pair, 4000 + g.dp_layer);
+      if (c.et == 0)
+        s.dp_ok = dp->world > 1
+                      ? int(dp_wait_geq(p, reinterpret_cast<const int*>(ob + dp->arrive_off) + dp_tl,
+                                        (p.dp_step + 1) * (dp->world - 1) * dp->pair, 4000 + g.dp_layer))
+                      : 1;
       epi_sync();
+      // A wait that ran out (the status word is set) leaves this tile's master
+      // shard and every rank's weight copy as they were: partial slots that are
+      // stale or half-written are never summed, nothing is broadcast and no
+      // arrival is counted, so the step fails without corrupting the weights.
+      dp_skip = s.dp_ok == 0;
     }
   }
   auto emit_out = [&](float (&vv)[32], int col0, int nvalid) {
@@ -825,6 +834,8 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
           bulk_commit();
         }
       }
+    } else if (dp_skip) {
+      // owner after a failed wait: the accumulator is only drained
     } else if (epi == PKT_EPI_WGRAD_SGD || dp_owner) {
       if (dp_owner) {
         // rank-ordered sum of the partials; this rank's own is v
@@ -963,7 +974,7 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
     if (c.et == 0) {
       if (!dp_owner)
         red_release_sys_add(peer_arrive, 1);
-      else
+      else if (!dp_skip)
         for (int r2 = 0; r2 < dp->world; ++r2)
           red_release_sys_add(reinterpret_cast<int*>(dp->base[r2] + dp->wready_off) + g.dp_layer, 1);
     }
@@ -1334,6 +1345,7 @@ __global__ void __launch_bounds__(kThreads, 1) pk_megakernel(const __grid_consta
   const uint32_t rank = P == 2 ? cluster_ctarank() : 0;
   unsigned long long* perf = p.perf ? p.perf + (size_t)blockIdx.x * PKT_PERF_WORDS : nullptr;
   const long long t_start = clock64();
+  const uint64_t g_start = (p.clock_acc && blockIdx.x == 0 && threadIdx.x == 0) ? globaltimer_ns() : 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NST; ++i) {
@@ -1394,36 +1406,88 @@ __global__ void __launch_bounds__(kThreads, 1) pk_megakernel(const __grid_consta
       tmem_dealloc(tmem_base, kTmemCols);
   }
   if (perf && threadIdx.x == 0) perf[kPerfTotal] = clock64() - t_start;
+  if (p.clock_acc && blockIdx.x == 0 && threadIdx.x == 0) {
+    // SM cycles and nanoseconds of CTA 0's lifetime (about the launch's):
+    // their ratio over many launches is the effective SM clock of a timed region
+    atomicAdd(p.clock_acc, static_cast<unsigned long long>(clock64() - t_start));
+    atomicAdd(p.clock_acc + 1, static_cast<unsigned long long>(globaltimer_ns() - g_start));
+    atomicAdd(p.clock_acc + 2, 1ull);
+  }
 }
 
 template <int P>
-cudaError_t launch_variant(const KParams& p, int blocks, cudaStream_t stream) {
-  // The attribute is per device; set it on every device this process launches on.
-  static unsigned long long attr_mask = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !(attr_mask & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(pk_megakernel<P>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<P>());
-    if (e != cudaSuccess) return e;
-    attr_mask |= 1ull << dev;
-  }
+cudaLaunchConfig_t make_config(int blocks, cudaStream_t stream, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(blocks);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem_bytes<P>();
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = P;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cfg;
+}
+
+// Per device: the shared-memory attribute is set once, and the number of CTAs
+// that can be resident at the same time (clusters x P) is looked up once.
+// Concurrent first launches from several host threads are serialised here.
+template <int P>
+cudaError_t prepare_variant(int dev, int* resident) {
+  static std::mutex mu;
+  static int cached[64] = {};
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (cached[dev] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(pk_megakernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         smem_bytes<P>());
+    if (e != cudaSuccess) return e;
+    int n = 0;
+    if (P == 1) {
+      int per_sm = 0, sms = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pk_megakernel<1>, kThreads, smem_bytes<1>());
+      if (e != cudaSuccess) return e;
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return e;
+      n = per_sm * sms;
+    } else {
+      cudaLaunchAttribute attr[1];
+      cudaLaunchConfig_t cfg = make_config<P>(P, nullptr, attr);
+      int clusters = 0;
+      e = cudaOccupancyMaxActiveClusters(&clusters, pk_megakernel<P>, &cfg);
+      if (e != cudaSuccess) return e;
+      n = clusters * P;
+    }
+    if (n <= 0) return cudaErrorInvalidConfiguration;
+    cached[dev] = n;
+  }
+  *resident = cached[dev];
+  return cudaSuccess;
+}
+
+template <int P>
+cudaError_t launch_variant(const KParams& p, int blocks, cudaStream_t stream) {
+  int dev = 0, resident = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = prepare_variant<P>(dev, &resident);
+  if (e != cudaSuccess) return e;
+  if (blocks > resident) return cudaErrorInvalidConfiguration;  // callers clamp first
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_config<P>(blocks, stream, attr);
   return cudaLaunchKernelEx(&cfg, pk_megakernel<P>, p);
 }
 
 }  // namespace
+
+cudaError_t max_resident_blocks(int pair, int* blocks) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  return pair == 2 ? prepare_variant<2>(dev, blocks) : prepare_variant<1>(dev, blocks);
+}
 
 cudaError_t launch_megakernel(const KParams& p, int blocks, cudaStream_t stream, int pair) {
   if (pair == 2) return launch_variant<2>(p, blocks, stream);

@@ -803,8 +803,12 @@ int Mlp::launch_list(pkt_task* d, int n, cudaStream_t st) {
     cudaMemsetAsync(rt->d_perf, 0, sizeof(unsigned long long) * PKT_PERF_WORDS * rt->perf_cap, st);
     kp.perf = rt->d_perf;
   }
-  rt->last_blocks = rt->num_sms & ~(P - 1);
-  e = launch_megakernel(kp, rt->num_sms & ~(P - 1), st, P);
+  kp.clock_acc = rt->d_clock;
+  int blocks = 0;
+  int rc = rt->clamp_blocks(rt->num_sms, P, &blocks);
+  if (rc) return rc;
+  rt->last_blocks = blocks;
+  e = launch_megakernel(kp, blocks, st, P);
   if (e != cudaSuccess) return cuda_fail(e, "launch megakernel");
   return PKT_OK;
 }
@@ -952,11 +956,17 @@ int pkt_mlp_load_batch(pkt_mlp* h, const void* x, const void* t, int on_device, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   const int q = m->next_slot;
-  cudaError_t e = cudaMemcpy2DAsync(m->Xs[q], size_t(m->ld[0]) * m->es, x, size_t(m->dims[0]) * m->es,
-                                    size_t(m->dims[0]) * m->es, m->B, kind, st);
+  // One linear copy per tensor when the device rows are unpadded (the common
+  // case: widths that are multiples of 64); a pitched copy only for padded rows.
+  auto copy_rows = [&](void* dst, const void* src, int width) -> cudaError_t {
+    const size_t row = size_t(width) * m->es;
+    const size_t pitch = size_t(pkb::round_up(width, 64)) * m->es;
+    if (pitch == row) return cudaMemcpyAsync(dst, src, row * m->B, kind, st);
+    return cudaMemcpy2DAsync(dst, pitch, src, row, row, m->B, kind, st);
+  };
+  cudaError_t e = copy_rows(m->Xs[q], x, m->dims[0]);
   if (e != cudaSuccess) return pkb::cuda_fail(e, "copy x");
-  e = cudaMemcpy2DAsync(m->Ts[q], size_t(m->ld[m->L]) * m->es, t, size_t(m->dims[m->L]) * m->es,
-                        size_t(m->dims[m->L]) * m->es, m->B, kind, st);
+  e = copy_rows(m->Ts[q], t, m->dims[m->L]);
   if (e != cudaSuccess) return pkb::cuda_fail(e, "copy target");
   m->active_slot = q;
   m->next_slot = q ^ 1;
@@ -1119,6 +1129,11 @@ int pkt_mlp_set_perf(pkt_mlp* h, int enabled) {
   if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
   h->m->rt->perf_enabled = enabled != 0;
   return PKT_OK;
+}
+
+int pkt_mlp_clock_stats(pkt_mlp* h, unsigned long long* out3, int reset) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  return h->m->rt->clock_stats(out3, reset != 0);
 }
 
 int pkt_mlp_fetch_perf(pkt_mlp* h, unsigned long long* out, int max_blocks, int* blocks) {

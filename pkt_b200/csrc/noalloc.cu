@@ -19,7 +19,10 @@
 //     it. Calls on one stream are ordered and safe;
 //   * the first call on a device looks up the array's device address
 //     (cudaGetSymbolAddress with that device current); make that first call
-//     before any stream capture.
+//     before any stream capture;
+//   * every wait inside the launch has a fixed budget of 2 s; what went wrong
+//     on the device (a timeout, a rejected task) stays in the array's status
+//     words until the next call, and pkt_axpy_noalloc_status reads it.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -69,6 +72,47 @@ __global__ void build_axpy_tasks(NoAllocScratch* s, const float* x, float* y, fl
 }  // namespace
 }  // namespace pkb
 
+namespace pkb {
+namespace {
+// Looks up (once per device, with that device current) the scratch array's
+// device address.
+int noalloc_scratch(NoAllocScratch** s, int* sms) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(PKT_ERR_ARGS, "device id out of range");
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_scratch_dev[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    e = cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    g_scratch_dev[dev] = static_cast<NoAllocScratch*>(ptr);
+  }
+  *s = g_scratch_dev[dev];
+  if (sms) *sms = g_num_sms[dev];
+  return PKT_OK;
+}
+}  // namespace
+}  // namespace pkb
+
+extern "C" int pkt_axpy_noalloc_status(int* code, int* task_index, int* detail) {
+  using namespace pkb;
+  NoAllocScratch* s = nullptr;
+  int rc = noalloc_scratch(&s, nullptr);
+  if (rc) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int h[4] = {0, 0, 0, 0};
+  e = cudaMemcpy(h, s->state, sizeof(h), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read no-alloc status words");
+  if (code) *code = h[1];
+  if (task_index) *task_index = h[2];
+  if (detail) *detail = h[3];
+  return PKT_OK;
+}
+
 extern "C" int pkt_axpy_noalloc(const float* x, float* y, float a, long long n, void* stream) {
   using namespace pkb;
   if (n < 0 || (n > 0 && (!x || !y))) return fail(PKT_ERR_ARGS, "bad axpy arguments");
@@ -77,30 +121,21 @@ extern "C" int pkt_axpy_noalloc(const float* x, float* y, float a, long long n, 
                 "pkt_axpy_noalloc: n=%lld exceeds the fixed scratch limit of %lld elements "
                 "(%d tasks of %lld); use pkt_axpy for larger arrays",
                 n, (long long)kNoAllocMaxTasks * kNoAllocChunk, kNoAllocMaxTasks, kNoAllocChunk);
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(PKT_ERR_ARGS, "device id out of range");
   NoAllocScratch* s = nullptr;
   int sms = 0;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_scratch_dev[dev]) {  // once per device, with that device current
-      void* ptr = nullptr;
-      e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
-      e = cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-      g_scratch_dev[dev] = static_cast<NoAllocScratch*>(ptr);
-    }
-    s = g_scratch_dev[dev];
-    sms = g_num_sms[dev];
-  }
+  int rc = noalloc_scratch(&s, &sms);  // once per device: the array's device address
+  if (rc) return rc;
   if (n == 0) return PKT_OK;
+  int resident = 0;
+  cudaError_t e = max_resident_blocks(1, &resident);
+  if (e != cudaSuccess) return cuda_fail(e, "occupancy of the persistent kernel");
+  if (sms > resident) sms = resident;
   const int ntask = int((n + kNoAllocChunk - 1) / kNoAllocChunk);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // one thread per task, and at least as many threads as status / token words to clear
   const int threads = 128;
-  const int blocks = (ntask > kStateHeader + 2 * kNoAllocTokens ? ntask : kStateHeader + 2) / threads + 1;
+  const int work = ntask > kStateHeader + 2 * kNoAllocTokens ? ntask : kStateHeader + 2 * kNoAllocTokens;
+  const int blocks = (work + threads - 1) / threads;
   build_axpy_tasks<<<blocks, threads, 0, st>>>(s, x, y, a, n, ntask);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch no-alloc task builder");

@@ -221,6 +221,8 @@ void Runtime::release() {
   cudaFree(d_gemms);
   cudaFree(d_counter);
   cudaFree(d_perf);
+  cudaFree(d_clock);
+  d_clock = nullptr;
   d_tasks = nullptr;
   d_state = nullptr;
   d_gemms = nullptr;
@@ -257,6 +259,38 @@ int Runtime::initialize(int max_tasks_) {
   if (!d_counter) {
     cudaError_t e = cudaMalloc(&d_counter, sizeof(unsigned long long));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(counter)");
+  }
+  if (!d_clock) {
+    cudaError_t e = cudaMalloc(&d_clock, 3 * sizeof(unsigned long long));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(clock words)");
+    e = cudaMemset(d_clock, 0, 3 * sizeof(unsigned long long));
+    if (e != cudaSuccess) return cuda_fail(e, "clear clock words");
+  }
+  return PKT_OK;
+}
+
+int Runtime::clamp_blocks(int blocks, int pair, int* out) {
+  cudaSetDevice(device);
+  int resident = 0;
+  cudaError_t e = max_resident_blocks(pair, &resident);
+  if (e != cudaSuccess) return cuda_fail(e, "occupancy of the persistent kernel");
+  if (blocks <= 0 || blocks > resident) blocks = resident;
+  if (pair == 2 && (blocks & 1)) blocks = blocks + 1 <= resident ? blocks + 1 : blocks - 1;
+  if (blocks <= 0) return fail(PKT_ERR_UNSUPPORTED, "no CTA of the persistent kernel fits on device %d", device);
+  *out = blocks;
+  return PKT_OK;
+}
+
+int Runtime::clock_stats(unsigned long long* out3, bool reset) {
+  cudaSetDevice(device);
+  if (!d_clock) return fail(PKT_ERR_ARGS, "runtime not initialized");
+  if (out3) {
+    cudaError_t e = cudaMemcpy(out3, d_clock, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "read clock words");
+  }
+  if (reset) {
+    cudaError_t e = cudaMemset(d_clock, 0, 3 * sizeof(unsigned long long));
+    if (e != cudaSuccess) return cuda_fail(e, "clear clock words");
   }
   return PKT_OK;
 }
@@ -302,8 +336,13 @@ int Runtime::reset_state(cudaStream_t stream, bool sync) {
 
 int Runtime::launch(int blocks, cudaStream_t stream) {
   cudaSetDevice(device);
-  if (blocks <= 0) blocks = num_sms;
   if (!d_state) return fail(PKT_ERR_ARGS, "runtime not initialized");
+  // pkt launches whatever grid it is given (include/runtime.hpp:175-228); a
+  // persistent grid larger than what fits at once is clamped here, and an odd
+  // count in pair mode is rounded to whole clusters.
+  if (blocks <= 0) blocks = num_sms;
+  int rc = clamp_blocks(blocks, cta_pair, &blocks);
+  if (rc) return rc;
   if (perf_enabled && blocks + 1 > perf_cap) {
     cudaFree(d_perf);
     cudaError_t e = cudaMalloc(&d_perf, sizeof(unsigned long long) * PKT_PERF_WORDS * (blocks + 1));
@@ -322,7 +361,7 @@ int Runtime::launch(int blocks, cudaStream_t stream) {
   p.task_counter = accounting ? d_counter : nullptr;
   p.perf = perf_enabled ? d_perf : nullptr;
   p.timeout_ns = timeout_ns;
-  if (cta_pair == 2 && (blocks & 1)) ++blocks;  // clusters of two (perf buffer has blocks + 1 rows)
+  p.clock_acc = d_clock;
   last_blocks = blocks;
   cudaError_t e = launch_megakernel(p, blocks, stream, cta_pair);
   if (e != cudaSuccess) return cuda_fail(e, "launch megakernel");
@@ -540,5 +579,10 @@ int pkt_runtime_fetch_perf(pkt_runtime* rt, unsigned long long* out, int max_blo
 }
 
 int pkt_runtime_last_launch_blocks(pkt_runtime* rt) { return rt ? rt->rt->last_blocks : 0; }
+
+int pkt_runtime_clock_stats(pkt_runtime* rt, unsigned long long* out3, int reset) {
+  if (!rt) return pkb::fail(PKT_ERR_ARGS, "null runtime");
+  return rt->rt->clock_stats(out3, reset != 0);
+}
 
 }  // extern "C"

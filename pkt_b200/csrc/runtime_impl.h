@@ -34,6 +34,7 @@ struct Runtime {
   bool perf_enabled = false;
   unsigned long long* d_perf = nullptr;
   int perf_cap = 0;
+  unsigned long long* d_clock = nullptr;  // [3]: SM cycles, ns, launches (KParams::clock_acc)
   int last_blocks = 0;
   unsigned long long timeout_ns = 2000000000ull;
   std::vector<int> segments;
@@ -51,6 +52,10 @@ struct Runtime {
   int launch(int blocks, cudaStream_t stream);
   int status(int* code, int* task, int* detail);
   int register_gemms(const pkt_gemm_desc* descs, int n, int* first);
+  // Clamps a persistent grid to the CTAs that fit on the device at once (and to
+  // whole clusters of `pair`); 0 or a negative count asks for the largest grid.
+  int clamp_blocks(int blocks, int pair, int* out);
+  int clock_stats(unsigned long long* out3, bool reset);
 };
 
 }  // namespace pkb

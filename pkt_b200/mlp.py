@@ -191,6 +191,13 @@ class MLP:
         check(self._L.pkt_mlp_status(self._h, ctypes.byref(code), ctypes.byref(task), ctypes.byref(detail)))
         return code.value, task.value, detail.value
 
+    def clock_stats(self, reset=False):
+        """(SM cycles, nanoseconds, launches) summed over the engine's launches since
+        the last reset; cycles * 1000 / ns is the mean SM clock in MHz."""
+        buf = (ctypes.c_ulonglong * 3)()
+        check(self._L.pkt_mlp_clock_stats(self._h, ctypes.cast(buf, c_void_p), int(reset)))
+        return int(buf[0]), int(buf[1]), int(buf[2])
+
     PERF_NAMES = ["tasks", "gemm_tiles", "ctrl_dep_wait", "ctrl_slot_wait", "load_stage_wait",
                   "mma_full_wait", "mma_tmem_wait", "epi_tmem_wait", "epi_gemm", "epi_simt", "total", "mma_slot_wait", "mma_issue",
                   "kblocks"]

@@ -257,3 +257,11 @@ def axpy_noalloc(x_ptr, y_ptr, a, n, stream=None):
     """pkt_axpy for callers that must not allocate: scratch in a fixed array of the
     library (n <= 67,108,864); calls that overlap on the GPU race on that array."""
     check(_lib.load().pkt_axpy_noalloc(x_ptr, y_ptr, float(a), int(n), stream))
+
+
+def axpy_noalloc_status():
+    """(code, task, detail) of the last pkt_axpy_noalloc launch on the current device
+    (all 0 after a clean run); synchronises the device first."""
+    code, task, detail = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    check(_lib.load().pkt_axpy_noalloc_status(ctypes.byref(code), ctypes.byref(task), ctypes.byref(detail)))
+    return code.value, task.value, detail.value

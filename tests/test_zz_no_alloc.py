@@ -22,7 +22,7 @@ def pk():
 
 @pytest.mark.parametrize("n", [1000, (1 << 22) + 5])
 def test_noalloc_matches_allocating_entry_point_twice(pk, n):
-    from pkt_b200.runtime import axpy, axpy_noalloc
+    from pkt_b200.runtime import axpy, axpy_noalloc, axpy_noalloc_status
     rng = np.random.default_rng(n)
     hx = rng.uniform(-1, 1, n).astype(np.float32)
     hy = rng.uniform(-1, 1, n).astype(np.float32)
@@ -31,6 +31,7 @@ def test_noalloc_matches_allocating_entry_point_twice(pk, n):
     for a in (2.5, -0.75):  # two calls in a row on the same buffers
         axpy(x.data_ptr(), y_ref.data_ptr(), a, n)
         axpy_noalloc(x.data_ptr(), y_new.data_ptr(), a, n)
+        assert axpy_noalloc_status() == (0, 0, 0)  # the launch's device status words
         assert np.array_equal(host(y_new), host(y_ref))
 
 
