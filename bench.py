@@ -49,8 +49,9 @@ def flops_per_sample(dims):
 # command, in the named profile.
 PROFILED_TRAFFIC = {
     "cfg2": {"bytes": 2.104e9 + 0.664e9,
-             "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one cfg2 step "
-                       "(profiles/megakernel_cfg2_bf16_b8192.md)"},
+             "source": "dram__bytes_read.sum + dram__bytes_write.sum of one pk_megakernel launch "
+                       "(one cfg2 step) in a separate ncu capture of this configuration; a fixed "
+                       "figure, not measured in this run"},
 }
 
 
@@ -123,8 +124,14 @@ class ClockSampler:
 
 
 def make_inputs(cfg, rank, seed=1234):
-    rng = np.random.default_rng(seed + rank)
     dims, B = cfg["dims"], cfg["batch"]
+    if cfg is CONFIGS["cfg1"]:
+        # train_linear's own recipe: mt19937(0), W ~ U(+-1/sqrt(in)), b = 0, targets
+        # from a fixed W*, b* ~ N(0, 1) plus N(0, 0.01^2) noise
+        from pkt_b200.data import make_linear_task
+        x, W, b, t = make_linear_task(dims[0], dims[1], B, seed=rank, noise=0.01)
+        return x, t, [W], [b]
+    rng = np.random.default_rng(seed + rank)
     x = rng.standard_normal((B, dims[0]), dtype=np.float32)
     if cfg is CONFIGS["cfg5"]:
         x = rng.uniform(-3, 3, (B, dims[0])).astype(np.float32)
@@ -139,37 +146,18 @@ def make_inputs(cfg, rank, seed=1234):
     return x, t, Ws, bs
 
 
-def cpu_sample_rate(cfg, rows, threads=0):
-    """The oracle (CPU restatement of pkt's host training loop, extended to the
-    MLP) timed on the box's host cores on two row counts of the same workload
-    (rows and 2*rows); one step = fixed part (weight rounding, SGD) + rows x
-    per-row part, extrapolated to the full batch. Returns (samples/s, threads,
-    seconds timed, description)."""
-    from oracle import oracle as orc
-    if threads:
-        orc.lib().orc_set_num_threads(threads)
-    nthreads = orc.lib().orc_num_threads()
-    B = cfg["batch"]
-    r1 = max(4, min(rows, B // 2))
-    r2 = 2 * r1
-    x, t, Ws, bs = make_inputs(dict(cfg, batch=r2), 0, seed=99)
-    mode = cfg["dtype"]
-    times = []
-    for r in (r1, r2):
-        t0 = time.perf_counter()
-        orc.mlp_train(cfg["dims"], x[:r], t[:r], Ws, bs, cfg["lr"], 1, mode=mode)
-        times.append(time.perf_counter() - t0)
-    per_row = max((times[1] - times[0]) / (r2 - r1), 1e-12)
-    fixed = max(times[0] - r1 * per_row, 0.0)
-    step_s = fixed + B * per_row
-    desc = (f"oracle step on {r1} and {r2} rows ({times[0]:.2f} s, {times[1]:.2f} s), "
-            f"extrapolated to the {B}-row batch: {fixed:.2f} s fixed + {per_row * 1e3:.2f} ms/row")
-    return B / step_s, nthreads, sum(times), desc
-
-
-def cpu_rows(cfg):
-    # about 5 s of single-step oracle work at the smaller row count on ~16 cores
-    return int(max(4, min(cfg["batch"] // 2, 5e10 / flops_per_sample(cfg["dims"]))))
+def cpu_full_batch(cfg, max_steps, budget_s, warmup=1):
+    """The fp32 OpenMP restatement of pkt's host training loop extended to the MLP
+    (oracle/cpu_mlp.cpp, built here with -O3 -march=native) on all host cores:
+    `warmup` untimed full-batch steps, then full-batch steps until `max_steps` or
+    `budget_s` seconds. Returns (result dict, description)."""
+    from oracle import cpu_baseline as cb
+    x, t, Ws, bs = make_inputs(cfg, 0)
+    r = cb.time_mlp(cfg["dims"], x, t, Ws, bs, cfg["lr"], max_steps, budget_s, warmup=warmup)
+    desc = (f"{r['steps']} full-batch step(s) of {cfg['batch']} rows timed ({r['seconds']:.2f} s) "
+            f"after {warmup} untimed; fp32 OpenMP restatement of pkt's host loop extended to the MLP "
+            f"({cb.FLAGS}), {r['threads']} threads on {os.cpu_count()} logical CPUs, {cb.cpu_model()}")
+    return r, desc
 
 
 def init_dist():
@@ -183,32 +171,31 @@ def run_reference(args, cfg_name, cfg):
     ws, rank, _ = init_dist()
     if rank != 0:
         return
-    # bounded sample per step: rows chosen so one step is ~1-3 s of CPU work
-    rows = cpu_rows(cfg)
-    rates = []
-    thr = 0
-    secs = 0.0
-    desc = ""
-    for i in range(min(args.warmup, 1) + max(args.steps, 1)):
-        r, thr, dt, desc = cpu_sample_rate(cfg, rows)
-        if i >= args.warmup:
-            rates.append(r)
-            secs += dt
-        if secs > 30:
-            break
-    v = float(np.mean(rates))
+    # full-batch steps, as many of the requested K as fit in about a minute
+    r, desc = cpu_full_batch(cfg, args.steps, 60.0, warmup=min(args.warmup, 1))
+    v = r["samples_per_s"]
     line = {
         "impl": "reference", "metric": "MLP train samples/s & % dense BF16 TC peak at 1/2/4/8 B200",
-        "value": v, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1000.0 * cfg["batch"] / v,
+        "value": v, "unit": "samples/s", "n_gpus": args.gpus, "steps": r["steps"],
+        "steps_requested": args.steps, "warmup": min(args.warmup, 1),
+        "ms_per_step": 1000.0 * cfg["batch"] / v,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": cfg["dtype"], "data": "synthetic (seeded N(0,1) inputs/targets, Kaiming-uniform weights)",
+        "dtype": "f32", "data": "synthetic (the same seeded inputs and weights as the GPU arm)",
         "config": {"workload": cfg_name + ": " + cfg["desc"], "global_batch": cfg["batch"],
                    "parallelism": "host CPU, OpenMP"},
-        "cpu_baseline": {"value": v, "unit": "samples/s", "cores": thr, "kind": "port",
-                         "sample": desc + f"; {len(rates)} timed repetitions, {secs:.1f} s"},
+        "cpu_baseline": {"value": v, "unit": "samples/s", "cores": r["threads"], "kind": "port",
+                         "sample": desc},
         "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "loss_first_last": [r["losses"][0], r["losses"][-1]],
     }
+    if cfg_name == "cfg1":
+        # pkt's own host loop (examples/train_linear.cu:101-151): single thread, no bias
+        from oracle import cpu_baseline as cb
+        x, t, Ws, _ = make_inputs(cfg, 0)
+        sps, secs, last = cb.time_pkt_loop(Ws[0], x, t, 100, cfg["lr"])
+        line["pkt_host_loop_1core"] = {"value": sps, "unit": "samples/s", "cores": 1,
+                                       "sample": f"100 steps of pkt's loop (no bias) in {secs:.3f} s",
+                                       "final_loss": last}
     print(json.dumps(line), flush=True)
 
 
@@ -308,6 +295,7 @@ def run_ours(args, cfg_name, cfg):
     torch.cuda.synchronize()
     sampler.start()
     time.sleep(0.3)
+    eng.clock_stats(reset=True)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     sampler.mark_begin()
     wall0 = time.perf_counter()
@@ -318,9 +306,21 @@ def run_ours(args, cfg_name, cfg):
     torch.cuda.synchronize()
     wall = time.perf_counter() - wall0
     sampler.mark_end()
+    kcyc, kns, klaunches = eng.clock_stats()
     if dist:
         dist.barrier()
     clocks = sampler.stop()
+    # effective SM clock of the timed launches: SM cycles / ns of CTA 0's lifetime,
+    # summed over every launch (nvidia-smi's 50 ms polling sees few samples of a
+    # short timed region)
+    smi_mhz = clocks.get("sm_mhz")
+    eff_mhz = kcyc * 1000.0 / kns if kns else None
+    clocks = {"sm_mhz": eff_mhz,
+              "sm_mhz_source": f"in-kernel clock64 / %globaltimer over CTA 0 of the {klaunches} timed launches",
+              "sm_max_mhz": clocks.get("sm_max_mhz") or measured_peaks()[0].get("sm_max_mhz"),
+              "reasons": clocks.get("reasons", []),
+              "smi_sm_mhz_median": smi_mhz, "smi_samples": clocks.get("samples", 0),
+              "power_w_median": clocks.get("power_w_median")}
     t_ms = evs[0].elapsed_time(evs[-1])
     per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
     losses = eng.losses()
@@ -385,7 +385,7 @@ def run_ours(args, cfg_name, cfg):
     # region ran at (nearly) full SM clock, the sustained (power-capped) figure
     # when the clocks sampled during it show the power cap holding them down.
     sm, smax = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
-    capped = sm is not None and smax and sm < 0.93 * smax
+    capped = bool(sm is not None and smax and sm < 0.93 * smax)
     peak = sustained if capped else burst
     traffic = PROFILED_TRAFFIC.get(cfg_name)
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -393,9 +393,10 @@ def run_ours(args, cfg_name, cfg):
                 "traffic": traffic["bytes"] if traffic else None,
                 "traffic_source": traffic["source"] if traffic else None,
                 "algorithmic_flop_per_launch": F,
-                "peak_kind": f"{peak_kind} " + ("bf16_tflops_sustained (SM clock held below max by "
-                                                "the power cap during the timed region)" if capped
-                                                else "bf16_tflops burst (timed region at full SM clock)"),
+                "peak_kind": f"{peak_kind} " + ("bf16_tflops_sustained (effective SM clock of the timed "
+                                                "launches below 93 % of max: power-capped)" if capped
+                                                else "bf16_tflops burst (timed launches at full SM clock)"),
+                "frac_of_burst": achieved / burst, "frac_of_sustained": achieved / sustained,
                 "kernel": "pk_megakernel (one launch = one training step)"}
     if rank != 0:
         return
@@ -427,9 +428,9 @@ def run_ours(args, cfg_name, cfg):
         "wall_s_timed": wall,
     }
     if ws == 1 and not args.no_cpu:
-        r, thr, dt, desc = cpu_sample_rate(cfg, cpu_rows(cfg))
-        line["cpu_baseline"] = {"value": r, "unit": "samples/s", "cores": thr, "kind": "port",
-                                "sample": desc}
+        r, desc = cpu_full_batch(cfg, 2, 10.0, warmup=1)
+        line["cpu_baseline"] = {"value": r["samples_per_s"], "unit": "samples/s",
+                                "cores": r["threads"], "kind": "port", "sample": desc}
     print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()

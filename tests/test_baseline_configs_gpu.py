@@ -1,0 +1,172 @@
+"""Parity at the exact configurations the benchmark plan names, against the fp64
+oracle on identical seeded inputs (the oracle's numpy restatement,
+oracle/mlp_np.py, which tests/test_oracle.py checks against oracle.cpp).
+
+  cfg2  4-layer ReLU MLP 1024-4096-4096-4096-1024, bf16 / fp32 accumulate, batch 8192
+        (the headline configuration): two steps, per-layer dW / db of each step and
+        the weights after them
+  cfg5  ragged 1000-3000-777-10, TF32, batch 4099, x ~ U(-3, 3), one-hot targets:
+        one step's gradients and a 20-step loss curve
+  cfg3  16 layers of width 512, bf16, batch 2048: one step's gradients of all 16
+        layers and a 20-step loss curve
+  cfg4  8 layers of width 8192, bf16: one step's gradients (batch 1024 per GPU
+        instead of 8192: same layer shapes, 8x less oracle work)
+  cfg1  pkt's train_linear problem with its own data recipe (mt19937(0),
+        W ~ U(+-1/sqrt(128)), targets from W*, b* ~ N(0, 1) plus N(0, 0.01^2)
+        noise), Linear 128->64 with bias, batch 256, TF32: 100 steps
+
+Tolerances (per tensor, max|a-b| / max|b|): bf16 2e-2, TF32 1e-3 after one step;
+loss curves within 1 % relative on every step.
+"""
+import numpy as np
+import pytest
+
+from oracle import mlp_np
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+from tests._gpu import rel_err, require_gpu  # noqa: E402
+
+TOL = {"bf16": 2e-2, "tf32": 1e-3}
+
+
+@pytest.fixture(scope="module")
+def pk():
+    require_gpu()
+    import pkt_b200
+    return pkt_b200
+
+
+def kaiming(rng, dims):
+    return [(rng.uniform(-1, 1, (dims[l + 1], dims[l])) * np.sqrt(6.0 / dims[l])).astype(np.float32)
+            for l in range(len(dims) - 1)]
+
+
+def normal_problem(dims, batch, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((batch, dims[0]), dtype=np.float32)
+    t = rng.standard_normal((batch, dims[-1]), dtype=np.float32)
+    Ws = kaiming(rng, dims)
+    bs = [rng.uniform(-0.05, 0.05, dims[l + 1]).astype(np.float32) for l in range(len(dims) - 1)]
+    return x, t, Ws, bs
+
+
+def engine(pk, dims, batch, dtype, lr, grad_mode, x, t, Ws, bs):
+    m = pk.MLP(dims, batch, dtype=dtype, lr=lr, bias=bs is not None, grad_mode=grad_mode)
+    m.set_params(Ws, bs)
+    m.load_batch(m.storage_array(x), m.storage_array(t))
+    return m
+
+
+def check_grads(m, ref, dtype, L):
+    dW, db = m.get_grads()
+    for l in range(L):
+        e = rel_err(dW[l], ref["dW"][l])
+        assert e < TOL[dtype], ("dW", l, e)
+        if ref["db"] is not None and ref["db"][l] is not None:
+            e = rel_err(db[l], ref["db"][l])
+            assert e < TOL[dtype], ("db", l, e)
+
+
+def test_cfg2_headline_two_steps(pk):
+    dims, B, lr = [1024, 4096, 4096, 4096, 1024], 8192, 1e-3
+    x, t, Ws, bs = normal_problem(dims, B, 21)
+    ref1 = mlp_np.mlp_train(dims, x, t, Ws, bs, lr, 1, mode="bf16", want_grads=True)
+    ref2 = mlp_np.mlp_train(dims, x, t, Ws, bs, lr, 2, mode="bf16", want_grads=True)
+    # gradients of step 1 and of step 2 (after one fused update), stored fp32
+    m = engine(pk, dims, B, "bf16", lr, 1, x, t, Ws, bs)
+    m.train(1)
+    check_grads(m, ref1, "bf16", 4)
+    m.train(1)
+    check_grads(m, ref2, "bf16", 4)
+    got = m.losses()
+    assert np.max(np.abs(got - ref2["losses"]) / ref2["losses"]) < 0.01, (got, ref2["losses"])
+    m.close()
+    # the fused path (SGD in the weight-gradient epilogue), as the benchmark runs it
+    m = engine(pk, dims, B, "bf16", lr, 0, x, t, Ws, bs)
+    m.train(2)
+    W2, b2 = m.get_params()
+    for l in range(4):
+        e = rel_err(W2[l] - Ws[l], ref2["W"][l] - Ws[l])
+        assert e < TOL["bf16"], ("W update", l, e)
+        e = rel_err(b2[l] - bs[l], ref2["b"][l] - bs[l])
+        assert e < TOL["bf16"], ("b update", l, e)
+    got = m.losses()
+    assert np.max(np.abs(got - ref2["losses"]) / ref2["losses"]) < 0.01
+    m.close()
+
+
+def cfg5_problem(seed):
+    dims, B = [1000, 3000, 777, 10], 4099
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(-3, 3, (B, dims[0])).astype(np.float32)
+    t = np.zeros((B, dims[-1]), np.float32)
+    t[np.arange(B), rng.integers(0, dims[-1], B)] = 1.0
+    Ws = kaiming(rng, dims)
+    bs = [np.zeros(dims[l + 1], np.float32) for l in range(3)]
+    return dims, B, x, t, Ws, bs
+
+
+def test_cfg5_ragged_tf32_gradients(pk):
+    dims, B, x, t, Ws, bs = cfg5_problem(22)
+    ref = mlp_np.mlp_train(dims, x, t, Ws, bs, 5e-3, 1, mode="tf32", want_grads=True)
+    m = engine(pk, dims, B, "tf32", 5e-3, 1, x, t, Ws, bs)
+    m.train(1)
+    check_grads(m, ref, "tf32", 3)
+    assert abs(m.losses()[0] - ref["losses"][0]) / ref["losses"][0] < 1e-3
+
+
+def test_cfg5_ragged_tf32_loss_curve(pk):
+    dims, B, x, t, Ws, bs = cfg5_problem(23)
+    steps = 20
+    ref = mlp_np.mlp_train(dims, x, t, Ws, bs, 5e-3, steps, mode="tf32")
+    m = engine(pk, dims, B, "tf32", 5e-3, 0, x, t, Ws, bs)
+    m.train(steps)
+    got = m.losses()
+    assert np.max(np.abs(got - ref["losses"]) / ref["losses"]) < 0.01
+    W1, _ = m.get_params()
+    for l in range(3):
+        assert rel_err(W1[l] - Ws[l], ref["W"][l] - Ws[l]) < 1e-2, l
+
+
+def test_cfg3_deep_narrow(pk):
+    dims, B, lr = [512] * 17, 2048, 1e-3
+    x, t, Ws, bs = normal_problem(dims, B, 24)
+    ref = mlp_np.mlp_train(dims, x, t, Ws, bs, lr, 1, mode="bf16", want_grads=True)
+    m = engine(pk, dims, B, "bf16", lr, 1, x, t, Ws, bs)
+    m.train(1)
+    check_grads(m, ref, "bf16", 16)
+    m.close()
+    steps = 20
+    ref = mlp_np.mlp_train(dims, x, t, Ws, bs, lr, steps, mode="bf16")
+    m = engine(pk, dims, B, "bf16", lr, 0, x, t, Ws, bs)
+    m.train(steps)
+    got = m.losses()
+    assert np.max(np.abs(got - ref["losses"]) / ref["losses"]) < 0.01
+    m.close()
+
+
+def test_cfg4_wide_layers_gradients(pk):
+    dims, B, lr = [8192] * 9, 1024, 1e-4
+    x, t, Ws, bs = normal_problem(dims, B, 25)
+    ref = mlp_np.mlp_train(dims, x, t, Ws, bs, lr, 1, mode="bf16", want_grads=True)
+    m = engine(pk, dims, B, "bf16", lr, 1, x, t, Ws, bs)
+    m.train(1)
+    check_grads(m, ref, "bf16", 8)
+    m.close()
+
+
+def test_cfg1_train_linear_with_its_data_recipe(pk):
+    x, W, b, t = orc.make_linear_task(128, 64, 256, seed=0, noise=0.01)
+    steps, lr = 100, 1e-2
+    ref = mlp_np.mlp_train([128, 64], x, t, [W], [b], lr, steps, mode="tf32")
+    m = engine(pk, [128, 64], 256, "tf32", lr, 0, x, t, [W], [b])
+    m.train(steps)
+    got = m.losses()
+    assert np.max(np.abs(got - ref["losses"]) / ref["losses"]) < 0.01
+    W1, b1 = m.get_params()
+    # 100 accumulated TF32 updates: the per-step 1e-3 bound compounds
+    assert rel_err(W1[0] - W, ref["W"][0] - W) < 1e-2
+    assert rel_err(b1[0] - b, ref["b"][0] - b) < 1e-2
+    m.close()

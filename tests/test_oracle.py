@@ -120,3 +120,36 @@ def test_oracle_axpy_is_fma():
 def test_bf16_round_is_rne():
     assert orc.lib().orc_bf16_round(1.0 + 2.0 ** -8) == 1.0  # tie -> even
     assert orc.lib().orc_bf16_round(1.0 + 3 * 2.0 ** -8) == 1.0 + 2.0 ** -6
+
+
+@pytest.mark.parametrize("mode", ["fp32", "tf32", "bf16"])
+def test_numpy_restatement_matches_c_oracle(mode):
+    """oracle/mlp_np.py (fp64 numpy GEMMs, used for the full-size configs) against
+    oracle.cpp's loops: gradients, losses and updated weights of two steps agree
+    to fp32 rounding of differently ordered fp64 sums (and the rare bf16 rounding
+    flip such a difference can cause)."""
+    from oracle import mlp_np
+    rng = np.random.default_rng(3)
+    dims, batch, lr = [48, 96, 40, 8], 70, 0.05
+    x = rng.standard_normal((batch, dims[0])).astype(np.float32)
+    t = rng.standard_normal((batch, dims[-1])).astype(np.float32)
+    Ws = [rng.uniform(-0.4, 0.4, (dims[i + 1], dims[i])).astype(np.float32) for i in range(3)]
+    bs = [rng.uniform(-0.1, 0.1, dims[i + 1]).astype(np.float32) for i in range(3)]
+    a = orc.mlp_train(dims, x, t, Ws, bs, lr, 2, mode=mode, want_grads=True)
+    b = mlp_np.mlp_train(dims, x, t, Ws, bs, lr, 2, mode=mode, want_grads=True)
+    tol = 1e-5 if mode != "bf16" else 2e-3
+    np.testing.assert_allclose(b["losses"], a["losses"], rtol=1e-5)
+    for l in range(3):
+        den = np.max(np.abs(a["dW"][l]))
+        assert np.max(np.abs(b["dW"][l] - a["dW"][l])) / den < tol, ("dW", l)
+        assert np.max(np.abs(b["db"][l] - a["db"][l])) / np.max(np.abs(a["db"][l])) < tol, ("db", l)
+        assert np.max(np.abs(b["W"][l] - a["W"][l])) < 1e-6, ("W", l)
+
+
+def test_numpy_rounding_helpers_match_c():
+    from oracle import mlp_np
+    rng = np.random.default_rng(4)
+    v = (rng.standard_normal(4096) * 10.0 ** rng.integers(-8, 8, 4096)).astype(np.float32)
+    got = mlp_np.bf16_round(v)
+    want = np.array([orc.lib().orc_bf16_round(float(f)) for f in v], np.float32)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
