@@ -232,6 +232,16 @@ int pkt_runtime_last_launch_blocks(pkt_runtime* rt);
  * launch; cycles * 1000 / ns is the mean SM clock in MHz. reset != 0 clears the
  * sums after reading them (out3 may be NULL to clear only). */
 int pkt_runtime_clock_stats(pkt_runtime* rt, unsigned long long* out3, int reset);
+/* Per-task trace of launches (no counterpart in pkt; its closest is the per-role
+ * PerfBlock cycle counters): when enabled, every launch records for each task
+ * PKT_TRACE_WORDS u64 = {CTA | opcode << 16 (GEMM tiles also: GEMM id << 32,
+ * tile_m & 255 << 48, tile_n & 255 << 56), then %globaltimer ns at: dequeue, dependencies
+ * satisfied, first TMA load issued, first MMA issued, last MMA committed, compute
+ * warps started (GEMM: accumulator complete), compute warps finished}; stages a
+ * task does not have stay 0. fetch copies the last launch's records (synchronous). */
+#define PKT_TRACE_WORDS 8
+int pkt_runtime_set_trace(pkt_runtime* rt, int enabled);
+int pkt_runtime_fetch_trace(pkt_runtime* rt, unsigned long long* out, int max_tasks, int* n);
 int pkt_num_sms(int device);
 const char* pkt_last_error(void);
 
@@ -331,6 +341,10 @@ int pkt_mlp_set_perf(pkt_mlp* m, int enabled);
 int pkt_mlp_fetch_perf(pkt_mlp* m, unsigned long long* out, int max_blocks, int* blocks);
 /* Effective SM clock of the engine's launches, as pkt_runtime_clock_stats. */
 int pkt_mlp_clock_stats(pkt_mlp* m, unsigned long long* out3, int reset);
+/* Per-task trace of the engine's launches, as pkt_runtime_set_trace / _fetch_trace
+ * (task indices are those of one step's task list). */
+int pkt_mlp_set_trace(pkt_mlp* m, int enabled);
+int pkt_mlp_fetch_trace(pkt_mlp* m, unsigned long long* out, int max_tasks, int* n);
 
 #ifdef __cplusplus
 }

@@ -53,10 +53,22 @@ def _mm(a, b):
     return np.matmul(a.astype(np.float64), b.astype(np.float64)).astype(np.float32)
 
 
-def mlp_train(dims, x, t, Ws, bs, lr, steps, mode="bf16", want_grads=False, relu_last=False):
+def _mm32(a, b):
+    """The same product accumulated in float32 (numpy's sgemm)."""
+    return np.matmul(np.asarray(a, np.float32), np.asarray(b, np.float32))
+
+
+def mlp_train(dims, x, t, Ws, bs, lr, steps, mode="bf16", want_grads=False, relu_last=False,
+              accum="fp64"):
     """Same contract as oracle.mlp_train (oracle.cpp orc_mlp_train).
 
+    accum="fp32" evaluates the same rounded arithmetic with float32 GEMM
+    accumulation, as any fp32-accumulating implementation does (the GPU's tensor
+    cores among them); the distance between the two evaluations is the
+    conditioning floor of a comparison against the fp64 truth.
+
     Returns dict(W, b, losses[, dW, db]) with the gradients of the last step."""
+    mm = _mm if accum == "fp64" else _mm32
     L = len(dims) - 1
     B = x.shape[0]
     W = [np.array(w, np.float32, copy=True) for w in Ws]
@@ -72,7 +84,7 @@ def mlp_train(dims, x, t, Ws, bs, lr, steps, mode="bf16", want_grads=False, relu
         Wop = [_operand(mode, w) for w in W]
         H = [H0]
         for l in range(L):
-            p = _mm(_operand(mode, H[l]), Wop[l].T)
+            p = mm(_operand(mode, H[l]), Wop[l].T)
             if b is not None:
                 p = p + b[l][None, :]
             if l < L - 1 or relu_last:
@@ -90,11 +102,11 @@ def mlp_train(dims, x, t, Ws, bs, lr, steps, mode="bf16", want_grads=False, relu
         db = [None] * L
         for l in range(L - 1, -1, -1):
             dYop = _operand(mode, dY)
-            dW[l] = _mm(dYop.T, _operand(mode, H[l]))
+            dW[l] = mm(dYop.T, _operand(mode, H[l]))
             if b is not None:
                 db[l] = np.sum(dY.astype(np.float64), axis=0).astype(np.float32)
             if l > 0:
-                v = _mm(dYop, Wop[l])
+                v = mm(dYop, Wop[l])
                 v = np.where(H[l] > 0, v, np.float32(0))
                 dY = _store(mode, v)
         nlr = np.float64(np.float32(-lr))

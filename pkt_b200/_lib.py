@@ -18,6 +18,7 @@ PKT_MAJOR_K, PKT_MAJOR_MN = 0, 1
 EPI_STORE, EPI_BIAS_ACT, EPI_MSE, EPI_DGRAD_RELU, EPI_WGRAD_SGD, EPI_WGRAD_STORE = range(6)
 DEV_OK, DEV_TIMEOUT_DEPS, DEV_TIMEOUT_PIPE, DEV_BAD_OPCODE, DEV_BAD_ARGS = range(5)
 PERF_WORDS = 16
+TRACE_WORDS = 8
 
 
 class PktError(RuntimeError):
@@ -83,6 +84,8 @@ _SIGS = {
     "pkt_runtime_fetch_perf": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
     "pkt_runtime_last_launch_blocks": ([_P], c_int),
     "pkt_runtime_clock_stats": ([_P, _P, c_int], c_int),
+    "pkt_runtime_set_trace": ([_P, c_int], c_int),
+    "pkt_runtime_fetch_trace": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
     "pkt_axpy": ([_P, _P, c_float, c_longlong, _P], c_int),
     "pkt_axpy_noalloc": ([_P, _P, c_float, c_longlong, _P], c_int),
     "pkt_axpy_noalloc_status": ([_P, _P, _P], c_int),
@@ -109,6 +112,8 @@ _SIGS = {
     "pkt_mlp_set_perf": ([_P, c_int], c_int),
     "pkt_mlp_fetch_perf": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
     "pkt_mlp_clock_stats": ([_P, _P, c_int], c_int),
+    "pkt_mlp_set_trace": ([_P, c_int], c_int),
+    "pkt_mlp_fetch_trace": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
 }
 
 EXPORTS = sorted(_SIGS)

@@ -106,6 +106,9 @@ struct alignas(128) DevGemm {
   CUtensorMap map_out;     // out: boxes of 32 columns x 32 rows (one compute warp's chunk)
   CUtensorMap map_w;       // w_out (fp32)
   CUtensorMap map_shadow;  // w_shadow (bf16)
+  CUtensorMap map_pf;      // the matrix the epilogue reads rows of (aux or w_in): L2 prefetch boxes
+  int pf_ok;               // 1: map_pf is valid (the loader prefetches each tile's box)
+  int pad_pf;
   CUtensorMap map_peer[PKT_DP_MAX_RANKS];  // WGRAD_PEER owner: w_shadow's twin on every rank
 };
 
@@ -163,7 +166,22 @@ struct KParams {
   int dp_step;        // fused data-parallel steps completed before this launch
   // optional [3]: += SM cycles, += nanoseconds of CTA 0's lifetime, += 1 per launch
   unsigned long long* clock_acc;
+  // optional [num_tasks][kTraceWords]: per task, %globaltimer stamps of its stages
+  unsigned long long* trace;
 };
+
+// Words of one task's trace record (pkt_mlp_fetch_trace / pkt_runtime_fetch_trace).
+enum TraceWord {
+  kTrCta = 0,       // bits 0-15 CTA, 16-31 opcode; GEMM tiles: 32-47 GEMM id, 48-55 tile_m, 56-63 tile_n (low 8 bits)
+  kTrDequeue = 1,   // controller took it from the queue
+  kTrReady = 2,     // its dependencies were satisfied (published to the slot ring)
+  kTrLoad = 3,      // loader issued its first TMA load (GEMM tiles)
+  kTrMma0 = 4,      // MMA issuer issued its first MMA (first stage had landed)
+  kTrMma1 = 5,      // MMA issuer committed its last MMA
+  kTrExec = 6,      // compute warps started it (GEMM: the accumulator was complete)
+  kTrDone = 7,      // compute warps finished it (before its token was published)
+};
+constexpr int kTraceWords = 8;
 
 constexpr int kStateHeader = 8;  // ints before the token counters
 inline int state_ints(int num_tokens) { return kStateHeader + 2 * num_tokens; }

@@ -168,8 +168,19 @@ __device__ void controller_loop(const KParams& p, SmemT<P>& s, unsigned long lon
       if (cursor_local >= cursor_end) break;
     }
     const int t = cursor_local++;
+    unsigned long long* tr = p.trace ? p.trace + (size_t)t * kTraceWords : nullptr;
+    if (tr) tr[kTrDequeue] = globaltimer_ns();
     pkt_task task;
     copy_task(&task, p.tasks + t);
+    if (tr) {
+      const pkt_gemm_tile_args* ga = reinterpret_cast<const pkt_gemm_tile_args*>(task.args);
+      const bool gemm = task.header.opcode == PKT_OP_GEMM;
+      tr[kTrCta] = (unsigned long long)blockIdx.x | ((unsigned long long)task.header.opcode << 16) |
+                   (gemm ? ((unsigned long long)(ga->gemm & 0xffffu) << 32) |
+                               ((unsigned long long)(ga->tile_m & 0xffu) << 48) |
+                               ((unsigned long long)(ga->tile_n & 0xffu) << 56)
+                         : 0ull);
+    }
     const pkt_task_header& h = task.header;
     if (!opcode_known(h.opcode)) {
       set_error(p, PKT_DEV_BAD_OPCODE, t, h.opcode);
@@ -225,6 +236,7 @@ __device__ void controller_loop(const KParams& p, SmemT<P>& s, unsigned long lon
     if (!wait_bar<(P == 2)>(p, &s.slot_empty[slot], ((seq / kSlots) & 1) ^ 1, 1)) break;
     slot_cycles += clock64() - c1;
     task.header.user_tag = uint32_t(t);
+    if (tr) tr[kTrReady] = globaltimer_ns();
     if (p.task_counter) atomicAdd(p.task_counter, 1ull);
     publish_slot<P>(s, slot, task);
     ++seq;
@@ -245,6 +257,16 @@ __device__ void controller_loop(const KParams& p, SmemT<P>& s, unsigned long lon
 }
 
 // ============================================================ loader (TMA producer)
+// The epilogue of a tile reads rows of a second matrix with plain loads (dgrad:
+// the activations for the ReLU mask; MSE: the targets; fused SGD: the fp32
+// master weights). Those rows are usually not in L2 (the activations were
+// written a whole forward pass earlier), so the loader asks for them at the tile
+// start: one TMA L2 prefetch of this CTA's 128-row box, landing while the
+// mainloop runs.
+__device__ __forceinline__ void prefetch_epilogue_rows(const DevGemm& g, int rblock, int tile_n) {
+  if (g.pf_ok) tma_prefetch_2d(&g.map_pf, tile_n * g.d.bn, rblock * kBM);
+}
+
 template <int P>
 __device__ void loader_loop(const KParams& p, SmemT<P>& s, uint32_t rank, unsigned long long* perf) {
   constexpr int NST = SmemT<P>::NST;
@@ -255,11 +277,13 @@ __device__ void loader_loop(const KParams& p, SmemT<P>& s, uint32_t rank, unsign
     const int slot = seq % kSlots;
     if (!wait_bar<(P == 2)>(p, &s.slot_full[slot], (seq / kSlots) & 1, 3, true)) break;
     const uint16_t op = s.slots[slot].header.opcode;
+    const uint32_t tix = s.slots[slot].header.user_tag;
     pkt_gemm_tile_args ga = *reinterpret_cast<const pkt_gemm_tile_args*>(s.slots[slot].args);
     release_slot<P>(s, slot, rank);
     ++seq;
     if (op == kOpStop) break;
     if (op != PKT_OP_GEMM) continue;
+    if (p.trace && rank == 0) p.trace[(size_t)tix * kTraceWords + kTrLoad] = globaltimer_ns();
     const DevGemm& g = p.gemms[ga.gemm];
     // Data of this tile was produced by other CTAs through generic stores and is
     // read here through the async proxy.
@@ -268,6 +292,7 @@ __device__ void loader_loop(const KParams& p, SmemT<P>& s, uint32_t rank, unsign
     // rows [rank*bn/2, +bn/2) of B; both CTAs' bytes count on the leader's barrier
     const int m0 = int(ga.tile_m) * kBM * P + int(rank) * kBM;
     const int n0 = int(ga.tile_n) * g.d.bn + int(rank) * g.b_rows;
+    prefetch_epilogue_rows(g, int(ga.tile_m) * P + int(rank), int(ga.tile_n));
     // per-tile constants in registers (the asm "memory" clobbers would force reloads)
     const int num_kb = g.num_kb, bk = g.bk, box_mn = g.box_mn;
     const bool a_kmaj = g.d.a_major == PKT_MAJOR_K, b_kmaj = g.d.b_major == PKT_MAJOR_K;
@@ -387,6 +412,7 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
     if (!wait_bar<(P == 2)>(p, &s.slot_full[slot], (seq / kSlots) & 1, 5, true)) break;
     slot_wait += clock64() - cs;
     const uint16_t op = s.slots[slot].header.opcode;
+    const uint32_t tix = s.slots[slot].header.user_tag;
     pkt_gemm_tile_args ga = *reinterpret_cast<const pkt_gemm_tile_args*>(s.slots[slot].args);
     if (elected) mbar_arrive(&s.slot_empty[slot]);  // the MMA issuer only runs in the leader CTA
     __syncwarp();
@@ -421,6 +447,7 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
       }
       const long long c2 = stamp(prof);
       full_wait += c2 - c1;
+      if (kb == 0 && p.trace && elected) p.trace[(size_t)tix * kTraceWords + kTrMma0] = globaltimer_ns();
       tc_fence_after();
       const uint32_t sa = smem_u32(s.stages[stage]);
       const uint32_t sb = sa + SmemT<P>::A_BYTES;
@@ -447,6 +474,7 @@ __device__ void mma_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base,
         mma_commit_pair_both(&s.tmem_full[acc]);  // accumulator complete in both CTAs
       else
         mma_commit(&s.tmem_full[acc]);
+      if (p.trace) p.trace[(size_t)tix * kTraceWords + kTrMma1] = globaltimer_ns();
     }
     __syncwarp();
     ++gemm_count;
@@ -646,11 +674,12 @@ __device__ bool dp_wait_geq(const KParams& p, const int* ctr, int target, int wh
 template <int P>
 __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, const DevGemm& g,
                               int tile_m, int tile_n, uint32_t tmem_base, uint32_t acc,
-                              uint32_t use, unsigned long long& tmem_wait) {
+                              uint32_t use, unsigned long long& tmem_wait, uint32_t tix) {
   const pkt_gemm_desc& d = g.d;
   const long long c0 = clock64();
   wait_bar(p, &s.tmem_full[acc], use & 1, 8);
   tmem_wait += clock64() - c0;
+  if (p.trace && c.et == 0 && c.rank == 0) p.trace[(size_t)tix * kTraceWords + kTrExec] = globaltimer_ns();
   __syncwarp();  // tcgen05.ld is warp-collective
   tc_fence_after();
 
@@ -723,15 +752,28 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
       dp_skip = s.dp_ok == 0;
     }
   }
+  // bf16 output chunks are 2 KB: three of them rotate through the warp's 6 KB
+  // staging area, so a chunk is staged while the two before it are still being
+  // stored; fp32 chunks (4 KB) use the area one at a time.
+  const bool rotate = out_dtype == PKT_DTYPE_BF16;
+  int stage_ix = 0;
   auto emit_out = [&](float (&vv)[32], int col0, int nvalid) {
     if (tma_out) {
-      if (c.lane == 0) bulk_wait_read_all();  // previous chunk's store has read the buffer
+      uint8_t* buf = stg;
+      if (rotate) {
+        buf = stg + stage_ix * 2048;
+        stage_ix = stage_ix == 2 ? 0 : stage_ix + 1;
+        if (c.lane == 0) bulk_wait_read<2>();  // the store 3 chunks back has read `buf`
+      } else if (c.lane == 0) {
+        bulk_wait_read_all();  // the previous chunk's store has read the buffer
+      }
       __syncwarp();
-      stage_row32(stg, out_dtype, c.lane, vv);
+      stage_row32(buf, out_dtype, c.lane, vv);
       fence_proxy_async_smem();
       __syncwarp();
-      if (c.lane == 0 && row0 < M && col0 < N) {
-        tma_store_2d(&g.map_out, stg, col0, row0);
+      if (c.lane == 0) {
+        // a group per chunk (possibly empty) keeps the group count = chunk count
+        if (row0 < M && col0 < N) tma_store_2d(&g.map_out, buf, col0, row0);
         bulk_commit();
       }
     } else {
@@ -740,6 +782,47 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
       if (nvalid > 0) store_row32(out, out_dtype, o, nvalid, vec, vv);
     }
   };
+
+  // The aux row segment (targets for MSE, activations for the ReLU mask) of
+  // chunk ch+1 is loaded into registers while chunk ch is processed: one chunk's
+  // worth of loads is always in flight (whole, aligned segments only; the rest
+  // take the plain per-chunk path).
+  const bool aux_rows = (epi == PKT_EPI_MSE || epi == PKT_EPI_DGRAD_RELU) && aux != nullptr;
+  uint4 auxq[4];
+  auto aux_issue = [&](int ch2) -> bool {
+    const int col = n0 + ch2 * 32;
+    // bf16 rows only (16 registers); fp32 aux rows take the per-chunk path
+    if (!aux_rows || in_es != 2 || !row_ok || min(N - col, bn - ch2 * 32) < 32) return false;
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(aux) +
+                                                      ((long long)row * ldaux + col) * in_es);
+    if (!aligned16(src)) return false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) auxq[i] = src[i];
+    return true;
+  };
+  // Chunk ch's aux values: from the registers loaded one chunk ahead, else loaded now.
+  auto aux_take = [&](bool ready, long long oa, int nvalid, float (&a)[32]) {
+    if (ready) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[8 * i + 0] = bf16_lo(auxq[i].x);
+        a[8 * i + 1] = bf16_hi(auxq[i].x);
+        a[8 * i + 2] = bf16_lo(auxq[i].y);
+        a[8 * i + 3] = bf16_hi(auxq[i].y);
+        a[8 * i + 4] = bf16_lo(auxq[i].z);
+        a[8 * i + 5] = bf16_hi(auxq[i].z);
+        a[8 * i + 6] = bf16_lo(auxq[i].w);
+        a[8 * i + 7] = bf16_hi(auxq[i].w);
+      }
+    } else if (nvalid > 0) {
+      const bool avec = aligned16(reinterpret_cast<const uint8_t*>(aux) + oa * in_es);
+      load_row32(aux, in_dtype, oa, nvalid, avec, a);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) a[j] = 0.f;
+    }
+  };
+  bool auxq_ready = aux_issue(0);
 
   // TMEM reads are double-buffered: chunk ch+1 is in flight while chunk ch is
   // processed and stored.
@@ -757,6 +840,7 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
     int nvalid = min(N - col0, bn - ch * 32);  // inside the matrix and inside this tile
     nvalid = nvalid < 0 ? 0 : (nvalid > 32 ? 32 : nvalid);
     if (!row_ok) nvalid = 0;
+
     // bias of the chunk's 32 columns: one coalesced load, broadcast by shuffles
     float bl = 0.f;
     if (add_bias && col0 + c.lane < N) bl = __ldg(bias + col0 + c.lane);
@@ -775,14 +859,8 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
       emit_out(v, col0, nvalid);
     } else if (epi == PKT_EPI_MSE) {
       float t[32];
-      const long long oa = (long long)row * ldaux + col0;
-      const bool avec = aligned16(reinterpret_cast<const uint8_t*>(aux) + oa * in_es);
-      if (nvalid > 0) {
-        load_row32(aux, in_dtype, oa, nvalid, avec, t);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) t[j] = 0.f;
-      }
+      aux_take(auxq_ready, (long long)row * ldaux + col0, nvalid, t);
+      auxq_ready = more ? aux_issue(ch + 1) : false;
       if (add_bias) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bl, j);
@@ -810,14 +888,8 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
       emit_out(v, col0, nvalid);
     } else if (epi == PKT_EPI_DGRAD_RELU) {
       float h[32];
-      const long long oa = (long long)row * ldaux + col0;
-      const bool avec = aligned16(reinterpret_cast<const uint8_t*>(aux) + oa * in_es);
-      if (nvalid > 0) {
-        load_row32(aux, in_dtype, oa, nvalid, avec, h);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) h[j] = 0.f;
-      }
+      aux_take(auxq_ready, (long long)row * ldaux + col0, nvalid, h);
+      auxq_ready = more ? aux_issue(ch + 1) : false;
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = (j < nvalid && h[j] > 0.f) ? v[j] : 0.f;
       emit_out(v, col0, nvalid);
@@ -1242,12 +1314,15 @@ __device__ void compute_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base, 
     const uint16_t op = task.header.opcode;
     if (op == kOpStop) break;
     const long long c0 = clock64();
+    unsigned long long* tr = (p.trace && c.et == 0 && c.rank == 0)
+                                 ? p.trace + (size_t)task.header.user_tag * kTraceWords : nullptr;
+    if (tr && op != PKT_OP_GEMM) tr[kTrExec] = globaltimer_ns();
     switch (op) {
       case PKT_OP_GEMM: {
         const pkt_gemm_tile_args& ga = *reinterpret_cast<const pkt_gemm_tile_args*>(task.args);
         const uint32_t acc = gemm_count & 1, use = gemm_count >> 1;
         epilogue_gemm<P>(p, s, c, p.gemms[ga.gemm], int(ga.tile_m), int(ga.tile_n), tmem_base, acc,
-                         use, tmem_wait);
+                         use, tmem_wait, task.header.user_tag);
         ++gemm_count;
         break;
       }
@@ -1299,6 +1374,7 @@ __device__ void compute_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base, 
       gemm_cycles += clock64() - c0;
     else
       simt_cycles += clock64() - c0;
+    if (tr) tr[kTrDone] = globaltimer_ns();
     // ---- publish completion: stores visible at gpu scope (and to the async
     // proxy of consumers' TMA loads) before the release on the token.
     __threadfence();

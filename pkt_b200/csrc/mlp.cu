@@ -179,6 +179,16 @@ struct Mlp {
     return bn;
   }
 
+  // Tile width of layer l's weight-gradient GEMM. The first layer's weight
+  // gradient is the last work of a step: its tiles are halved in width (when
+  // they are 256 wide) so the step ends on finer tasks and the SMs finish closer
+  // together.
+  int wgrad_bn(int l) const {
+    int bn = pick_bn(dims[l + 1], dims[l], true);
+    if (l == 0 && L > 1 && bn == 256 && P == 2) bn = 128;
+    return bn;
+  }
+
   int alloc(void** p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, std::max<size_t>(bytes, 16));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(mlp buffer)");
@@ -285,7 +295,7 @@ int Mlp::setup_dp() {
   bias_total = 0;
   for (int l = 0; l < L; ++l) {
     const int M = dims[l + 1], N = dims[l];
-    wg_bn[l] = pick_bn(M, N, true);
+    wg_bn[l] = wgrad_bn(l);
     wg_tm[l] = (M + kBM * P - 1) / (kBM * P);
     wg_tn[l] = (N + wg_bn[l] - 1) / wg_bn[l];
     wg_base[l] = wg_total;
@@ -453,7 +463,7 @@ int Mlp::build(int p, int q) {
     d.b = Hin(l, q);
     d.ldb = ld[l];
     d.b_major = PKT_MAJOR_MN;
-    d.bn = pick_bn(d.M, d.N, true);
+    d.bn = wgrad_bn(l);
     if (grad_mode == 2) {
       // the owner of a tile applies SGD to its master shard and writes the bf16
       // copy the next step reads (locally here, on the other ranks in the kernel)
@@ -807,6 +817,8 @@ int Mlp::launch_list(pkt_task* d, int n, cudaStream_t st) {
   int blocks = 0;
   int rc = rt->clamp_blocks(rt->num_sms, P, &blocks);
   if (rc) return rc;
+  rc = rt->trace_for(n, st, &kp.trace);
+  if (rc) return rc;
   rt->last_blocks = blocks;
   e = launch_megakernel(kp, blocks, st, P);
   if (e != cudaSuccess) return cuda_fail(e, "launch megakernel");
@@ -1129,6 +1141,17 @@ int pkt_mlp_set_perf(pkt_mlp* h, int enabled) {
   if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
   h->m->rt->perf_enabled = enabled != 0;
   return PKT_OK;
+}
+
+int pkt_mlp_set_trace(pkt_mlp* h, int enabled) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  h->m->rt->trace_enabled = enabled != 0;
+  return PKT_OK;
+}
+
+int pkt_mlp_fetch_trace(pkt_mlp* h, unsigned long long* out, int max_tasks, int* n) {
+  if (!h || !out || !n) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  return h->m->rt->fetch_trace(out, max_tasks, n);
 }
 
 int pkt_mlp_clock_stats(pkt_mlp* h, unsigned long long* out3, int reset) {

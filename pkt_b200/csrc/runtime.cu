@@ -104,6 +104,28 @@ bool make_store_map(CUtensorMap* map, const void* base, int dtype, long long col
   return r == CUDA_SUCCESS;
 }
 
+// Tensor map for L2 prefetches of the rows a tile's epilogue reads: one box =
+// `box_cols` columns x 128 rows, no swizzle (a prefetch never lands in shared
+// memory). False where TMA cannot address the matrix (the epilogue then just
+// reads without the prefetch).
+static bool make_prefetch_map(CUtensorMap* map, const void* base, int dtype, long long cols,
+                              long long rows, long long ld, int box_cols) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc || base == nullptr || box_cols <= 0 || box_cols > 256) return false;
+  const int es = dtype == PKT_DTYPE_BF16 ? 2 : 4;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * es) % 16 != 0 || (box_cols * es) % 16 != 0)
+    return false;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld * es)};
+  cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(kBM)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int gemm_tiles(const pkt_gemm_desc& d, int* tm, int* tn) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0 || d.bn < 16 || d.bn > kMaxBN || d.bn % 16 != 0)
     return fail(PKT_ERR_ARGS, "GEMM shape M=%d N=%d K=%d bn=%d invalid", d.M, d.N, d.K, d.bn);
@@ -208,6 +230,11 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
       g->tma_out = make_store_map(&g->map_out, d.out, d.out_dtype, d.N, d.M, d.ldo);
     }
   }
+  if (d.epilogue == PKT_EPI_MSE || d.epilogue == PKT_EPI_DGRAD_RELU)
+    g->pf_ok = make_prefetch_map(&g->map_pf, d.aux, d.in_dtype == PKT_DTYPE_BF16 ? PKT_DTYPE_BF16 : PKT_DTYPE_F32,
+                                 d.N, d.M, d.ldaux, d.bn);
+  else if (d.epilogue == PKT_EPI_WGRAD_SGD || d.epilogue == PKT_EPI_WGRAD_PEER)
+    g->pf_ok = make_prefetch_map(&g->map_pf, d.w_in, PKT_DTYPE_F32, d.N, d.M, d.ldw, d.bn);
   return PKT_OK;
 }
 
@@ -223,6 +250,9 @@ void Runtime::release() {
   cudaFree(d_perf);
   cudaFree(d_clock);
   d_clock = nullptr;
+  cudaFree(d_trace);
+  d_trace = nullptr;
+  trace_cap = 0;
   d_tasks = nullptr;
   d_state = nullptr;
   d_gemms = nullptr;
@@ -278,6 +308,34 @@ int Runtime::clamp_blocks(int blocks, int pair, int* out) {
   if (pair == 2 && (blocks & 1)) blocks = blocks + 1 <= resident ? blocks + 1 : blocks - 1;
   if (blocks <= 0) return fail(PKT_ERR_UNSUPPORTED, "no CTA of the persistent kernel fits on device %d", device);
   *out = blocks;
+  return PKT_OK;
+}
+
+int Runtime::trace_for(int n, cudaStream_t stream, unsigned long long** out) {
+  *out = nullptr;
+  if (!trace_enabled) return PKT_OK;
+  if (n > trace_cap) {
+    cudaFree(d_trace);
+    d_trace = nullptr;
+    trace_cap = 0;
+    cudaError_t e = cudaMalloc(&d_trace, sizeof(unsigned long long) * kTraceWords * std::max(1, n));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(trace)");
+    trace_cap = std::max(1, n);
+  }
+  cudaError_t e = cudaMemsetAsync(d_trace, 0, sizeof(unsigned long long) * kTraceWords * std::max(1, n), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "clear trace");
+  trace_tasks = n;
+  *out = d_trace;
+  return PKT_OK;
+}
+
+int Runtime::fetch_trace(unsigned long long* out, int max_tasks, int* n) {
+  cudaSetDevice(device);
+  if (!d_trace) return fail(PKT_ERR_ARGS, "no traced launch (enable tracing first)");
+  const int k = std::min(max_tasks, trace_tasks);
+  cudaError_t e = cudaMemcpy(out, d_trace, sizeof(unsigned long long) * kTraceWords * k, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read trace");
+  *n = k;
   return PKT_OK;
 }
 
@@ -362,6 +420,8 @@ int Runtime::launch(int blocks, cudaStream_t stream) {
   p.perf = perf_enabled ? d_perf : nullptr;
   p.timeout_ns = timeout_ns;
   p.clock_acc = d_clock;
+  rc = trace_for(num_tasks, stream, &p.trace);
+  if (rc) return rc;
   last_blocks = blocks;
   cudaError_t e = launch_megakernel(p, blocks, stream, cta_pair);
   if (e != cudaSuccess) return cuda_fail(e, "launch megakernel");
@@ -579,6 +639,17 @@ int pkt_runtime_fetch_perf(pkt_runtime* rt, unsigned long long* out, int max_blo
 }
 
 int pkt_runtime_last_launch_blocks(pkt_runtime* rt) { return rt ? rt->rt->last_blocks : 0; }
+
+int pkt_runtime_set_trace(pkt_runtime* rt, int enabled) {
+  if (!rt) return pkb::fail(PKT_ERR_ARGS, "null runtime");
+  rt->rt->trace_enabled = enabled != 0;
+  return PKT_OK;
+}
+
+int pkt_runtime_fetch_trace(pkt_runtime* rt, unsigned long long* out, int max_tasks, int* n) {
+  if (!rt || !out || !n) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  return rt->rt->fetch_trace(out, max_tasks, n);
+}
 
 int pkt_runtime_clock_stats(pkt_runtime* rt, unsigned long long* out3, int reset) {
   if (!rt) return pkb::fail(PKT_ERR_ARGS, "null runtime");

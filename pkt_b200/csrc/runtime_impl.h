@@ -35,6 +35,10 @@ struct Runtime {
   unsigned long long* d_perf = nullptr;
   int perf_cap = 0;
   unsigned long long* d_clock = nullptr;  // [3]: SM cycles, ns, launches (KParams::clock_acc)
+  bool trace_enabled = false;
+  unsigned long long* d_trace = nullptr;  // [trace_cap][kTraceWords]
+  int trace_cap = 0;
+  int trace_tasks = 0;  // tasks of the last traced launch
   int last_blocks = 0;
   unsigned long long timeout_ns = 2000000000ull;
   std::vector<int> segments;
@@ -56,6 +60,9 @@ struct Runtime {
   // whole clusters of `pair`); 0 or a negative count asks for the largest grid.
   int clamp_blocks(int blocks, int pair, int* out);
   int clock_stats(unsigned long long* out3, bool reset);
+  // Trace buffer for a launch of n tasks (cleared on `stream`); null when tracing is off.
+  int trace_for(int n, cudaStream_t stream, unsigned long long** out);
+  int fetch_trace(unsigned long long* out, int max_tasks, int* n);
 };
 
 }  // namespace pkb

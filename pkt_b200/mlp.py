@@ -198,6 +198,20 @@ class MLP:
         check(self._L.pkt_mlp_clock_stats(self._h, ctypes.cast(buf, c_void_p), int(reset)))
         return int(buf[0]), int(buf[1]), int(buf[2])
 
+    TRACE_NAMES = ["cta", "dequeue", "ready", "load", "mma0", "mma1", "exec", "done"]
+
+    def set_trace(self, enabled=True):
+        """Record per-task stage timestamps of every launch (pkt_mlp_set_trace)."""
+        check(self._L.pkt_mlp_set_trace(self._h, int(enabled)))
+
+    def fetch_trace(self):
+        """Records of the last launch: uint64 array [tasks, 8] (see TRACE_NAMES)."""
+        n_max = self.step_info()["tasks"]
+        buf = np.zeros((max(n_max, 1), _lib.TRACE_WORDS), np.uint64)
+        got = c_int()
+        check(self._L.pkt_mlp_fetch_trace(self._h, buf.ctypes.data_as(c_void_p), n_max, ctypes.byref(got)))
+        return buf[:got.value]
+
     PERF_NAMES = ["tasks", "gemm_tiles", "ctrl_dep_wait", "ctrl_slot_wait", "load_stage_wait",
                   "mma_full_wait", "mma_tmem_wait", "epi_tmem_wait", "epi_gemm", "epi_simt", "total", "mma_slot_wait", "mma_issue",
                   "kblocks"]
