@@ -45,6 +45,8 @@ __global__ void f32_to_bf16_2d(const float* src, int rows, int cols, int lds, ui
 
 inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
+
+
 // grad_mode 2: copies the fp32 master rows/cols of one weight tile from its
 // owner's exchange region (a peer mapping) into this rank's copy.
 __global__ void gather_master_tile(const float* src, float* dst, int rows, int cols, int ld) {
@@ -170,8 +172,12 @@ struct Mlp {
     int bn = std::min(cap, need);
     bn = std::max(align, bn / align * align);
     const int tiles_m = (M + kBM * P - 1) / (kBM * P);
-    // shrink the tile until the GEMM alone fills the SMs (small layers)
-    while (bn > std::max(64 * P, align) && (long long)tiles_m * ((N + bn - 1) / bn) < rt->num_sms) {
+    // Narrower tiles only for GEMMs too small to give half of the CTAs (pairs) a
+    // tile: the step's other GEMMs fill the rest, while a narrower tile has a
+    // shorter k-block, which the stage ring (sized in bytes for the widest tile)
+    // covers for less time, so its MMAs stall on loads.
+    const int units = std::max(1, rt->num_sms / P);
+    while (bn > std::max(64 * P, align) && 2LL * tiles_m * ((N + bn - 1) / bn) < units) {
       const int nb = bn / 2;
       if (nb % align != 0) break;
       bn = nb;
@@ -179,15 +185,8 @@ struct Mlp {
     return bn;
   }
 
-  // Tile width of layer l's weight-gradient GEMM. The first layer's weight
-  // gradient is the last work of a step: its tiles are halved in width (when
-  // they are 256 wide) so the step ends on finer tasks and the SMs finish closer
-  // together.
-  int wgrad_bn(int l) const {
-    int bn = pick_bn(dims[l + 1], dims[l], true);
-    if (l == 0 && L > 1 && bn == 256 && P == 2) bn = 128;
-    return bn;
-  }
+  // Tile width of layer l's weight-gradient GEMM.
+  int wgrad_bn(int l) const { return pick_bn(dims[l + 1], dims[l], true); }
 
   int alloc(void** p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, std::max<size_t>(bytes, 16));
@@ -556,6 +555,11 @@ int Mlp::build(int p, int q) {
       tl.push_back(t);
     }
   }
+  // Forward: layer by layer, row block by row block. (Listing the layers as an
+  // interleaved wavefront was measured slower: a row block's input has to be
+  // complete when it is dequeued, and with every controller running up to
+  // kSlots tasks ahead of its pipeline that needs hundreds of tiles of distance
+  // in the list, which leaves little to interleave.)
   for (int l = 0; l < L; ++l) {
     const DevGemm& dg = G(fwd[l]);
     for (int i = 0; i < TM; ++i)
@@ -575,50 +579,63 @@ int Mlp::build(int p, int q) {
         ++tiles;
       }
   }
-  {
-    const DevGemm& dg = G(fwd[L - 1]);
-    pkt_task t{};
-    t.header.opcode = PKT_OP_LOSS_REDUCE;
-    pkt_loss_reduce_args a{loss_partials, losses, dg.tiles_m * P * dg.tiles_n,
-                           float(1.0 / (double(B) * double(dims[L]))), step_ctr};
-    t.header.arg_bytes = sizeof(a);
-    std::memcpy(t.args, &a, sizeof(a));
-    t.header.buffer_read_id = uint16_t(BF[L - 1]);
-    t.header.wait_count = uint32_t(TM * dg.tiles_n);
-    tl.push_back(t);
-  }
   if (grad_mode != 2) {
-    // The dgrad chain (the critical path) first, row block by row block; the
-    // weight-gradient tiles, which only need a complete dY_l, after it: by the time
-    // a CTA dequeues them their inputs are normally complete, so the controller
-    // rarely blocks on a token.
-    for (int l = L - 1; l >= 1; --l) {
-      const DevGemm& dg = G(dgr[l]);
-      for (int i = 0; i < TM; ++i)
-        for (int j = 0; j < dg.tiles_n; ++j) {
-          pkt_task t = gemm_task(dgr[l], i, j);
-          t.header.buffer_read_id = uint16_t(Bk[l][i]);
-          t.header.wait_count = uint32_t(dy_tn[l]);
-          t.header.buffer_write_id = uint16_t(Bk[l - 1][i]);
-          t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
-          tl.push_back(t);
-          ++tiles;
-        }
-    }
-    for (int l = L - 1; l >= 0; --l) {
+    // The dgrad chain (the critical path) first, layer by layer, row block by
+    // row block. The last layer's weight-gradient tiles need only the complete
+    // dY_{L-1}, which the forward's last tiles finish: they are spread over the
+    // dgrad tiles, from a distance of four grid waves after the forward on (long
+    // K = batch mainloops between the short ones of a K = d_L dgrad layer, whose
+    // epilogues would otherwise hold the MMA issuer). The other layers' weight-
+    // gradient tiles, which need a complete dY_l, follow the whole dgrad chain:
+    // by the time a CTA dequeues them their inputs are normally complete.
+    auto wgrad_order = [&](int l) {
       const DevGemm& wg = G(wgr[l]);
       // groups of 8 tile rows swept column by column: the tiles in flight share
       // fewer operand blocks, so more of them stay in L2
+      std::vector<std::pair<int, int>> order;
       for (int i0 = 0; i0 < wg.tiles_m; i0 += 8)
         for (int j = 0; j < wg.tiles_n; ++j)
-          for (int i = i0; i < std::min(wg.tiles_m, i0 + 8); ++i) {
-            pkt_task t = gemm_task(wgr[l], i, j);
-            t.header.buffer_read_id = uint16_t(BF[l]);
-            t.header.wait_count = uint32_t(TM * dy_tn[l]);
-            t.header.buffer_write_id = uint16_t(WG_base + l);
-            tl.push_back(t);
-            ++tiles;
-          }
+          for (int i = i0; i < std::min(wg.tiles_m, i0 + 8); ++i) order.push_back({i, j});
+      return order;
+    };
+    auto emit_wgrad = [&](int l, int i, int j) {
+      pkt_task t = gemm_task(wgr[l], i, j);
+      t.header.buffer_read_id = uint16_t(BF[l]);
+      t.header.wait_count = uint32_t(TM * dy_tn[l]);
+      t.header.buffer_write_id = uint16_t(WG_base + l);
+      tl.push_back(t);
+      ++tiles;
+    };
+    auto emit_dgrad = [&](int l, int i) {
+      const DevGemm& dg = G(dgr[l]);
+      for (int j = 0; j < dg.tiles_n; ++j) {
+        pkt_task t = gemm_task(dgr[l], i, j);
+        t.header.buffer_read_id = uint16_t(Bk[l][i]);
+        t.header.wait_count = uint32_t(dy_tn[l]);
+        t.header.buffer_write_id = uint16_t(Bk[l - 1][i]);
+        t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
+        tl.push_back(t);
+        ++tiles;
+      }
+    };
+    const std::vector<std::pair<int, int>> wlast = wgrad_order(L - 1);
+    size_t wnext = 0;
+    long long dgrad_tiles = 0, dgrad_listed = 0;
+    for (int l = L - 1; l >= 1; --l) dgrad_tiles += (long long)TM * G(dgr[l]).tiles_n;
+    const long long start = 4LL * std::max(1, rt->num_sms / P);
+    for (int l = L - 1; l >= 1; --l)
+      for (int i = 0; i < TM; ++i) {
+        emit_dgrad(l, i);
+        dgrad_listed += G(dgr[l]).tiles_n;
+        if (dgrad_listed < start || dgrad_tiles <= start) continue;
+        const long long want = (long long)wlast.size() * (dgrad_listed - start) / (dgrad_tiles - start);
+        for (; (long long)wnext < want && wnext < wlast.size(); ++wnext)
+          emit_wgrad(L - 1, wlast[wnext].first, wlast[wnext].second);
+      }
+    for (int l = L - 1; l >= 0; --l) {
+      const std::vector<std::pair<int, int>> order = wgrad_order(l);
+      for (size_t k = (l == L - 1 ? wnext : 0); k < order.size(); ++k)
+        emit_wgrad(l, order[k].first, order[k].second);
       if (has_bias) {
         const int n = dims[l + 1];
         for (int c0 = 0; c0 < n; c0 += 512) {
@@ -728,6 +745,20 @@ int Mlp::build(int p, int q) {
         tl.push_back(t);
       }
     }
+  }
+  {
+    // last in the list: the MSE tiles it sums finished long before, so it never
+    // holds a CTA waiting
+    const DevGemm& dg = G(fwd[L - 1]);
+    pkt_task t{};
+    t.header.opcode = PKT_OP_LOSS_REDUCE;
+    pkt_loss_reduce_args a{loss_partials, losses, dg.tiles_m * P * dg.tiles_n,
+                           float(1.0 / (double(B) * double(dims[L]))), step_ctr};
+    t.header.arg_bytes = sizeof(a);
+    std::memcpy(t.args, &a, sizeof(a));
+    t.header.buffer_read_id = uint16_t(BF[L - 1]);
+    t.header.wait_count = uint32_t(TM * dg.tiles_n);
+    tl.push_back(t);
   }
   gemm_tiles_per_step = tiles;
 

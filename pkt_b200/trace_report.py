@@ -100,8 +100,9 @@ def analyse(tr, dims):
 
 
 def print_report(rep):
+    mhz = rep.get("sm_mhz")
     print(f"launch {rep['launch_us']:.1f} us, {rep['tasks']} tasks, {rep['gemm_tiles']} GEMM tiles, "
-          f"{rep['ctas']} MMA issuers")
+          f"{rep['ctas']} MMA issuers" + (f", SM clock {mhz:.0f} MHz" if mhz else ""))
     print(f"{'gemm':>8} {'tiles':>6} {'mma us':>8} {'load->mma':>10} {'epilogue':>9} {'ready->done':>12}")
     for name, d in rep["gemms"].items():
         print(f"{name:>8} {d['tiles']:6d} {d['mma_us']:8.2f} {d['load_to_mma_us']:10.2f} "
@@ -141,10 +142,13 @@ def main():
     m.load_batch(m.storage_array(x), m.storage_array(t))
     m.train(args.warmup)
     m.set_trace(True)
+    m.clock_stats(reset=True)
     m.train(1)
     tr = m.fetch_trace()
+    cyc, ns, _ = m.clock_stats()
     m.set_trace(False)
     rep = analyse(tr, dims)
+    rep["sm_mhz"] = cyc * 1000.0 / ns if ns else None
     print(f"dims {dims} batch {args.batch} {args.dtype}")
     print_report(rep)
     if args.json:
