@@ -281,8 +281,10 @@ typedef struct pkt_mlp_config {
                        inspection); 2: fused data parallel over peer memory
                        (pkt_mlp_dp_handle / pkt_mlp_dp_connect) */
   int max_bn;       /* largest tile N to use (0: 256) */
-  int cta_pair;     /* 0 or 2: CTA pairs share 256-row tiles (tcgen05 cta_group::2);
-                       1: every CTA computes its own 128-row tiles */
+  int cta_pair;     /* 2: CTA pairs share 256-row tiles (tcgen05 cta_group::2);
+                       1: every CTA computes its own 128-row tiles; 0: automatic
+                       (pairs when the widest layer gives every pair a 256 x 256
+                       tile, single CTAs for narrow, latency-bound networks) */
 } pkt_mlp_config;
 
 int pkt_mlp_create(int device, const pkt_mlp_config* cfg, pkt_mlp** out);

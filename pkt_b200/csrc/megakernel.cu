@@ -208,9 +208,9 @@ __device__ void controller_loop(const KParams& p, SmemT<P>& s, unsigned long lon
       bool ok = true;
       while (true) {
         bool ready = true;
-        if (r1 != 0) {
+        if (r1 != 0) {  // (epochs start at 0: a zero read_epoch needs no second load)
           ready = ld_acquire_gpu(tok_count(p) + r1) >= int(h.wait_count) &&
-                  ld_acquire_gpu(tok_epoch(p) + r1) >= int(h.read_epoch);
+                  (h.read_epoch == 0 || ld_acquire_gpu(tok_epoch(p) + r1) >= int(h.read_epoch));
         }
         if (ready && r2 != 0) ready = ld_acquire_gpu(tok_count(p) + r2) >= int(h.ext_wait_count);
         if (ready) break;
@@ -1375,11 +1375,14 @@ __device__ void compute_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base, 
     else
       simt_cycles += clock64() - c0;
     if (tr) tr[kTrDone] = globaltimer_ns();
-    // ---- publish completion: stores visible at gpu scope (and to the async
-    // proxy of consumers' TMA loads) before the release on the token.
-    __threadfence();
+    // ---- publish completion. Every thread's stores are ordered before the
+    // barrier; thread 0 then makes them visible at gpu scope with one fence
+    // (cumulative over what the barrier ordered before it) and releases the
+    // token. The proxy fence orders this thread's async-proxy (TMA store) writes,
+    // complete by now, with the generic release.
     fence_proxy_async_global();
     epi_sync();
+    if (c.et == 0) __threadfence();
     if (P == 2 && c.et == 0) {
       // pair: the leader publishes once the other CTA's half is stored too
       const int ps = (seq - 1) % kSlots;

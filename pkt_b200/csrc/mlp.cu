@@ -45,6 +45,11 @@ __global__ void f32_to_bf16_2d(const float* src, int rows, int cols, int lds, ui
 
 inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
+// Training steps one launch runs when pkt_mlp_train is asked for that many or
+// more (grad_mode 0; even, so the weight parity after the launch is the one
+// before it).
+constexpr int kMultiSteps = 4;
+
 
 
 // grad_mode 2: copies the fp32 master rows/cols of one weight tile from its
@@ -101,6 +106,11 @@ struct Mlp {
   // step task lists by [weight parity][input slot]; update lists by weight parity
   std::vector<pkt_task> tasks[2][2], update[2];
   pkt_task* d_tasks[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
+  // kMultiSteps consecutive steps in one launch (grad_mode 0), by starting weight
+  // parity and input slot; empty when not built
+  std::vector<pkt_task> multi[2][2];
+  pkt_task* d_multi[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
+  int wg_token_base = 0;  // token of layer 0's weight-gradient tiles (layer l: + l)
   pkt_task* d_update[2] = {nullptr, nullptr};
   int num_tokens = 0;
   int gemm_tiles_per_step = 0;
@@ -128,6 +138,8 @@ struct Mlp {
       F(Ts[k]);
       F(d_tasks[k][0]);
       F(d_tasks[k][1]);
+      F(d_multi[k][0]);
+      F(d_multi[k][1]);
     }
     for (auto p : H) F(p);
     for (auto p : dY) F(p);
@@ -196,6 +208,7 @@ struct Mlp {
   }
 
   int setup(const pkt_mlp_config& c);
+  int build_multi();
   int setup_dp();
   int connect(int rank, int world, const uint8_t* handles);
   int build(int p, int q);
@@ -222,7 +235,19 @@ int Mlp::setup(const pkt_mlp_config& c) {
     return fail(PKT_ERR_UNSUPPORTED, "fused data parallel (grad_mode 2) needs bf16 weights");
   ld.resize(L + 1);
   for (int l = 0; l <= L; ++l) ld[l] = round_up(dims[l], 64);
-  P = c.cta_pair == 1 ? 1 : 2;
+  if (c.cta_pair == 1 || c.cta_pair == 2) {
+    P = c.cta_pair;
+  } else {
+    // Automatic: CTA pairs (256-row tiles, half the operand traffic per SM) when
+    // the widest layer alone gives every pair a 256 x 256 tile; single CTAs
+    // otherwise -- a narrow network is bound by the latency of its layer chain,
+    // which a pair lengthens (both CTAs' loads land before the MMA starts, and
+    // the pair hands its completion over before publishing it).
+    long long widest = 0;
+    for (int l = 0; l < L; ++l)
+      widest = std::max(widest, (long long)((B + 255) / 256) * ((dims[l + 1] + 255) / 256));
+    P = widest >= rt->num_sms / 2 ? 2 : 1;
+  }
   TM = (B + kBM * P - 1) / (kBM * P);
   TMr = TM * P;
   int rc;
@@ -523,6 +548,7 @@ int Mlp::build(int p, int q) {
   for (int i = 0; i < TM; ++i) Bk[L - 1][i] = F[L - 1][i];
   for (int l = 0; l < L; ++l) BF[l] = next_id++;
   const int WG_base = next_id;
+  wg_token_base = WG_base;
   next_id += L;
   std::vector<int> WR(L, 0);  // grad_mode 2: this step's weights of layer l have arrived
   if (grad_mode == 2)
@@ -622,19 +648,32 @@ int Mlp::build(int p, int q) {
     size_t wnext = 0;
     long long dgrad_tiles = 0, dgrad_listed = 0;
     for (int l = L - 1; l >= 1; --l) dgrad_tiles += (long long)TM * G(dgr[l]).tiles_n;
-    const long long start = 4LL * std::max(1, rt->num_sms / P);
-    for (int l = L - 1; l >= 1; --l)
+    const int units = std::max(1, rt->num_sms / P);
+    const long long start = 4LL * units;
+    // A layer whose weight gradient is only a few tiles (a narrow, latency-bound
+    // network) has them listed right after its dgrad tiles instead: dY_l is then
+    // complete or nearly so, the few CTAs that take them wait at most one layer,
+    // and the weight gradients overlap the rest of the dgrad chain instead of
+    // following it.
+    auto small_wgrad = [&](int l) { return G(wgr[l]).tiles_m * G(wgr[l]).tiles_n * 2 <= units; };
+    std::vector<char> wg_done(L, 0);
+    for (int l = L - 1; l >= 1; --l) {
       for (int i = 0; i < TM; ++i) {
         emit_dgrad(l, i);
         dgrad_listed += G(dgr[l]).tiles_n;
-        if (dgrad_listed < start || dgrad_tiles <= start) continue;
+        if (small_wgrad(L - 1) || dgrad_listed < start || dgrad_tiles <= start) continue;
         const long long want = (long long)wlast.size() * (dgrad_listed - start) / (dgrad_tiles - start);
         for (; (long long)wnext < want && wnext < wlast.size(); ++wnext)
           emit_wgrad(L - 1, wlast[wnext].first, wlast[wnext].second);
       }
+      if (small_wgrad(l)) {
+        for (const auto& ij : wgrad_order(l)) emit_wgrad(l, ij.first, ij.second);
+        wg_done[l] = 1;
+      }
+    }
     for (int l = L - 1; l >= 0; --l) {
       const std::vector<std::pair<int, int>> order = wgrad_order(l);
-      for (size_t k = (l == L - 1 ? wnext : 0); k < order.size(); ++k)
+      for (size_t k = (l == L - 1 ? wnext : 0); k < order.size() && !wg_done[l]; ++k)
         emit_wgrad(l, order[k].first, order[k].second);
       if (has_bias) {
         const int n = dims[l + 1];
@@ -818,6 +857,68 @@ int Mlp::build(int p, int q) {
   return rt->ensure_tokens(num_tokens);
 }
 
+// kMultiSteps steps in one launch (grad_mode 0): the single-step lists of
+// alternating weight parity, each step on its own range of dependency tokens.
+// Every weight-gradient tile, bias-update and loss-reduce task of a step also
+// counts on one "step done" token, which the next step's first-layer forward
+// tiles read. That covers every task of the step: the weight-gradient tiles need
+// every dgrad tile (dY_0 needs the whole dgrad chain) and every forward tile
+// (dY_{L-1} needs the whole forward) -- so the next step neither reads weights
+// before their update nor overwrites activations, gradients or loss partials the
+// step still reads. It saves the launch, the token reset and the ramp-up /
+// drain of the persistent grid between steps.
+int Mlp::build_multi() {
+  for (int p = 0; p < 2; ++p)
+    for (int q = 0; q < 2; ++q) {
+      multi[p][q].clear();
+      cudaFree(d_multi[p][q]);
+      d_multi[p][q] = nullptr;
+    }
+  if (grad_mode != 0) return PKT_OK;
+  const int T = num_tokens + 1;  // tokens per step: the step's own plus its "step done"
+  if ((long long)kMultiSteps * T > 65535) return PKT_OK;  // single-step launches only
+  for (int p = 0; p < 2; ++p)
+    for (int q = 0; q < 2; ++q) {
+      std::vector<pkt_task>& ml = multi[p][q];
+      int done_count = 0;  // tasks of one step that count on its "step done" token
+      for (int k = 0; k < kMultiSteps; ++k) {
+        const std::vector<pkt_task>& one = tasks[(p + k) & 1][q];
+        const int off = k * T, done = off + num_tokens;
+        int count = 0;
+        auto shift = [&](uint32_t id) { return id == 0 ? 0u : id + uint32_t(off); };
+        for (const pkt_task& t0 : one) {
+          pkt_task t = t0;
+          pkt_task_header& h = t.header;
+          const bool wgrad = h.opcode == PKT_OP_GEMM && h.buffer_write_id >= wg_token_base &&
+                             h.buffer_write_id < wg_token_base + L;
+          h.buffer_read_id = uint16_t(shift(h.buffer_read_id));
+          h.buffer_write_id = uint16_t(shift(h.buffer_write_id));
+          h.ext_ids = shift(h.ext_ids & 0xffffu) | (shift(h.ext_ids >> 16) << 16);
+          if (wgrad) {  // the per-layer token nothing else reads becomes the step's
+            h.buffer_write_id = uint16_t(done);
+            ++count;
+          } else if ((h.opcode == PKT_OP_BIAS_SGD || h.opcode == PKT_OP_LOSS_REDUCE) &&
+                     h.buffer_write_id == 0) {
+            h.buffer_write_id = uint16_t(done);
+            ++count;
+          }
+          if (k > 0 && h.opcode == PKT_OP_GEMM && h.buffer_read_id == 0) {
+            // a first-layer forward tile: after the whole previous step
+            h.buffer_read_id = uint16_t(done - T);
+            h.wait_count = uint32_t(done_count);
+          }
+          ml.push_back(t);
+        }
+        done_count = count;
+      }
+      cudaError_t e = cudaMalloc(&d_multi[p][q], sizeof(pkt_task) * ml.size());
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(multi-step tasks)");
+      e = cudaMemcpy(d_multi[p][q], ml.data(), sizeof(pkt_task) * ml.size(), cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) return cuda_fail(e, "copy multi-step tasks");
+    }
+  return rt->ensure_tokens(kMultiSteps * T);
+}
+
 int Mlp::launch_list(pkt_task* d, int n, cudaStream_t st) {
   rt->num_tokens = rt->token_cap;
   cudaError_t e = cudaMemsetAsync(rt->d_state, 0, sizeof(int) * state_ints(rt->num_tokens), st);
@@ -871,7 +972,7 @@ static int rebuild(Mlp* m) {
       int rc = m->build(p, q);
       if (rc) return rc;
     }
-  return PKT_OK;
+  return m->build_multi();
 }
 
 extern "C" {
@@ -1025,8 +1126,16 @@ int pkt_mlp_train(pkt_mlp* h, int steps, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (m->grad_mode == 2 && m->dp_world == 0)
     return pkb::fail(PKT_ERR_ARGS, "grad_mode 2: call pkt_mlp_dp_connect before training");
-  for (int s = 0; s < steps; ++s) {
+  for (int s = 0; s < steps;) {
     const int p = m->parity, q = m->active_slot;
+    if (steps - s >= pkb::kMultiSteps && m->d_multi[p][q]) {
+      int rc = m->launch_list(m->d_multi[p][q], int(m->multi[p][q].size()), st);
+      if (rc) return rc;
+      s += pkb::kMultiSteps;
+      m->losses_enqueued += pkb::kMultiSteps;
+      continue;  // kMultiSteps is even: the parity is unchanged
+    }
+    ++s;
     int rc = m->launch_list(m->d_tasks[p][q], int(m->tasks[p][q].size()), st);
     if (rc) return rc;
     if (m->grad_mode == 2) m->dp_step++;

@@ -34,7 +34,7 @@ def from_bf16_bits(h):
 
 class MLP:
     def __init__(self, dims, batch, dtype="bf16", lr=1e-3, bias=True, relu_last=False,
-                 grad_mode=0, max_bn=0, cta_pair=2, device=None):
+                 grad_mode=0, max_bn=0, cta_pair=0, device=None):
         L = _lib.load()
         self._L = L
         self.dims = list(dims)

@@ -121,7 +121,7 @@ def main():
     ap.add_argument("--batch", type=int, default=8192)
     ap.add_argument("--dtype", default="bf16")
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--cta-pair", type=int, default=2)
+    ap.add_argument("--cta-pair", type=int, default=0)
     ap.add_argument("--json", default=None)
     args = ap.parse_args()
     if "x" in args.dims:
