@@ -13,6 +13,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <fstream>
 #include <cstdlib>
 #include <cstring>
 #include <iostream>
@@ -94,11 +95,81 @@ float cpu_train(std::vector<float> W, const std::vector<float>& x, const std::ve
 
 struct Opts {
   int m = 1024, n = 1024, batch = 64, steps = 20, fwd_tm = 2, fwd_tn = 128, bwd_tm = 64, bwd_tn = 128;
-  int blocks = -1;
+  int blocks = -1, repeats = 1, seg_window = 0;
   float lr = 1e-3f;
   bool skip_cpu = false, check_loss = false, check_tasks = false, bias = false;
-  std::string engine = "tasks", dtype = "tf32", layers;
+  bool perf = false, print_profile = false;
+  std::string engine = "tasks", dtype = "tf32", layers, perf_json;
 };
+
+// Per-role summary of the per-CTA counters of one launch (pkt's --perf report,
+// examples/train_linear.cu:724-895), in ms per step averaged over CTAs (cycles
+// converted with the launch's measured SM clock), and --perf-json.
+int report_perf(const std::vector<pk::PerfBlock>& blocks, double sm_mhz, float step_ms, int steps,
+                const Opts& o) {
+  if (blocks.empty()) {
+    std::cerr << "Failed to fetch perf counters.\n";
+    return 3;
+  }
+  pk::PerfBlock tot{};
+  unsigned long long tmin = ~0ull, tmax = 0;
+  for (const pk::PerfBlock& b : blocks) {
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(&b);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(&tot);
+    for (size_t i = 0; i < sizeof(pk::PerfBlock) / 8; ++i) dst[i] += src[i];
+    tmin = std::min(tmin, b.tasks_issued);
+    tmax = std::max(tmax, b.tasks_issued);
+  }
+  const double nb = double(blocks.size());
+  auto ms = [&](unsigned long long cyc) { return double(cyc) / nb / (sm_mhz * 1e3) / steps; };
+  struct Row {
+    const char* name;
+    unsigned long long cyc;
+  };
+  const Row rows[] = {{"controller.deps_wait", tot.ctrl_wait_cycles},
+                      {"controller.slot_wait", tot.ctrl_slot_wait_cycles},
+                      {"loader.stage_wait", tot.load_wait_slot_cycles},
+                      {"mma.stage_wait", tot.mma_full_wait_cycles},
+                      {"mma.accumulator_wait", tot.mma_tmem_wait_cycles},
+                      {"mma.issue", tot.mma_issue_cycles},
+                      {"compute.accumulator_wait", tot.compute_wait_loaded_cycles},
+                      {"compute.gemm_epilogue", tot.compute_work_cycles},
+                      {"compute.elementwise", tot.simt_work_cycles},
+                      {"total", tot.total_cycles}};
+  std::cout << "\nPer-role counters (averaged per CTA, per step; SM clock " << sm_mhz << " MHz):\n";
+  std::cout << "  blocks: " << blocks.size() << "  steps: " << steps << "  step_ms: " << step_ms << "\n";
+  std::cout << "  tasks per CTA: min " << tmin << " max " << tmax << "  GEMM tiles: " << tot.gemm_tiles << "\n";
+  for (const Row& r : rows) {
+    const double v = ms(r.cyc);
+    std::cout << "  " << r.name << ": " << v << " ms (" << (step_ms > 0 ? 100.0 * v / step_ms : 0.0) << "%)\n";
+  }
+  if (!o.perf_json.empty()) {
+    std::ofstream out(o.perf_json);
+    if (!out) {
+      std::cerr << "Failed to open --perf-json path: " << o.perf_json << "\n";
+      return 3;
+    }
+    out << "{\n  \"blocks\": " << blocks.size() << ",\n  \"step_ms\": " << step_ms
+        << ",\n  \"sm_mhz\": " << sm_mhz << ",\n  \"tasks_completed_min\": " << tmin
+        << ",\n  \"tasks_completed_max\": " << tmax << ",\n  \"ratios\": {\n"
+        << "    \"ctrl_wait_frac\": " << (tot.total_cycles ? double(tot.ctrl_wait_cycles) / tot.total_cycles : 0.0)
+        << ",\n    \"mma_issue_frac\": " << (tot.total_cycles ? double(tot.mma_issue_cycles) / tot.total_cycles : 0.0)
+        << ",\n    \"compute_work_frac\": "
+        << (tot.total_cycles ? double(tot.compute_work_cycles + tot.simt_work_cycles) / tot.total_cycles : 0.0)
+        << "\n  },\n  \"totals\": {\n";
+    static const char* names[] = {"tasks_issued", "gemm_tiles", "ctrl_wait_cycles", "ctrl_slot_wait_cycles",
+                                  "load_wait_slot_cycles", "mma_full_wait_cycles", "mma_tmem_wait_cycles",
+                                  "compute_wait_loaded_cycles", "compute_work_cycles", "simt_work_cycles",
+                                  "total_cycles", "mma_slot_wait_cycles", "mma_issue_cycles", "kblocks",
+                                  "mma_gap_cycles", "mma_lifetime_cycles"};
+    const unsigned long long* v = reinterpret_cast<const unsigned long long*>(&tot);
+    for (int i = 0; i < 16; ++i) out << "    \"" << names[i] << "\": " << v[i] << (i < 15 ? ",\n" : "\n");
+    out << "  }\n}\n";
+  }
+  return 0;
+}
+
+double clock_mhz(const unsigned long long c[3]) { return c[1] ? double(c[0]) * 1e3 / double(c[1]) : 0.0; }
 
 bool parse(int argc, char** argv, Opts& o) {
   for (int i = 1; i < argc; ++i) {
@@ -121,12 +192,17 @@ bool parse(int argc, char** argv, Opts& o) {
     else if (a == "--engine") o.engine = val();
     else if (a == "--dtype") o.dtype = val();
     else if (a == "--layers") o.layers = val();
+    else if (a == "--repeats") o.repeats = std::atoi(val());
+    else if (a == "--seg-window") o.seg_window = std::atoi(val());
+    else if (a == "--perf") o.perf = true;
+    else if (a == "--perf-json") { o.perf = true; o.perf_json = val(); }
+    else if (a == "--print-profile") { o.perf = true; o.print_profile = true; }
     else {
       std::cerr << "Unknown arg " << a << "\n";
       return false;
     }
   }
-  return o.m > 0 && o.n > 0 && o.batch > 0 && o.steps > 0 && o.fwd_tm > 0 && o.fwd_tn > 0 &&
+  return o.m > 0 && o.n > 0 && o.batch > 0 && o.steps > 0 && o.repeats > 0 && o.fwd_tm > 0 && o.fwd_tn > 0 &&
          o.bwd_tm > 0 && o.bwd_tn > 0 && (o.engine == "tasks" || o.engine == "mlp");
 }
 
@@ -195,16 +271,36 @@ int run_tasks(const Opts& o, std::vector<float>& W, const std::vector<float>& x,
   pk::Runtime rt;
   rt.initialize(int(tasks.size()));
   rt.set_task_accounting_enabled(o.check_tasks);
-  rt.submit_tasks(tasks);
+  rt.set_perf_enabled(o.perf);
+  if (o.seg_window > 0) rt.set_segment_window_size(o.seg_window);
   cudaEvent_t a, b;
   cudaEventCreate(&a);
   cudaEventCreate(&b);
-  cudaEventRecord(a);
-  rt.launch(o.blocks > 0 ? o.blocks : pk::Runtime::get_num_sms());
-  cudaEventRecord(b);
-  rt.synchronize();
-  cudaEventElapsedTime(&ms, a, b);
-  int rc = rt.last_error();
+  // --repeats: the whole task list again from the same starting weights; the
+  // fastest launch is reported (pkt reports per repeat)
+  const std::vector<float> W0 = W;
+  ms = 0.f;
+  int rc = PKT_OK;
+  for (int rep = 0; rep < o.repeats && rc == PKT_OK; ++rep) {
+    if (rep) cudaMemcpy(dW, W0.data(), W0.size() * 4, cudaMemcpyHostToDevice);
+    rt.submit_tasks(tasks);
+    pkt_runtime_clock_stats(rt.handle(), nullptr, 1);
+    cudaEventRecord(a);
+    rt.launch(o.blocks > 0 ? o.blocks : pk::Runtime::get_num_sms());
+    cudaEventRecord(b);
+    rt.synchronize();
+    float t = 0.f;
+    cudaEventElapsedTime(&t, a, b);
+    ms = rep == 0 ? t : std::min(ms, t);
+    rc = rt.last_error();
+  }
+  if (!rc && o.perf) {
+    unsigned long long clk[3] = {0, 0, 0};
+    pkt_runtime_clock_stats(rt.handle(), clk, 0);
+    std::vector<pk::PerfBlock> blocks;
+    rt.fetch_perf_blocks(blocks);
+    rc = report_perf(blocks, clock_mhz(clk), ms / o.steps, o.steps, o);
+  }
   if (rc != PKT_OK) std::cerr << "runtime error: " << rt.last_error_string() << "\n";
   if (!rc && o.check_tasks) {
     unsigned long long issued = 0;
@@ -238,7 +334,7 @@ int run_mlp(const Opts& o, std::vector<float>& W, const std::vector<float>& x,
   const int L = int(dims.size()) - 1;
   const bool bf = o.dtype == "bf16";
   pkt_mlp_config cfg{L, dims.data(), o.batch, bf ? PKT_DTYPE_BF16 : PKT_DTYPE_TF32, o.bias ? 1 : 0, 0, o.lr,
-                     0, 0, 2};
+                     0, 0, 0};
   int dev = 0;
   cudaGetDevice(&dev);
   pkt_mlp* h = nullptr;
@@ -278,11 +374,25 @@ int run_mlp(const Opts& o, std::vector<float>& W, const std::vector<float>& x,
   cudaEvent_t a, b;
   cudaEventCreate(&a);
   cudaEventCreate(&b);
+  if (o.perf) pkt_mlp_set_perf(h, 1);
+  pkt_mlp_clock_stats(h, nullptr, 1);
   cudaEventRecord(a);
   int rc = pkt_mlp_train(h, o.steps, nullptr);
   cudaEventRecord(b);
   cudaEventSynchronize(b);
   cudaEventElapsedTime(&ms, a, b);
+  if (!rc && o.perf) {
+    // the counters cover the last launch: one step, or the last group of steps
+    // the engine ran in one launch
+    unsigned long long clk[3] = {0, 0, 0};
+    pkt_mlp_clock_stats(h, clk, 0);
+    std::vector<pk::PerfBlock> blocks(1024);
+    int got = 0;
+    pkt_mlp_fetch_perf(h, reinterpret_cast<unsigned long long*>(blocks.data()), int(blocks.size()), &got);
+    blocks.resize(size_t(got));
+    const int per_launch = clk[2] ? int(o.steps / clk[2]) : 1;
+    rc = report_perf(blocks, clock_mhz(clk), ms / o.steps, per_launch > 0 ? per_launch : 1, o);
+  }
   losses.resize(o.steps);
   int got = 0;
   if (!rc) rc = pkt_mlp_losses(h, losses.data(), o.steps, &got);
@@ -299,7 +409,8 @@ int main(int argc, char** argv) {
   if (!parse(argc, argv, o)) {
     std::cerr << "usage: train_linear [--m M] [--n N] [--batch B] [--steps S] [--lr LR] "
                  "[--fwd-tile-m/n T] [--bwd-tile-m/n T] [--blocks K] [--skip-cpu] [--check-loss] "
-                 "[--check-tasks] [--engine tasks|mlp] [--dtype tf32|bf16] [--bias] [--layers n,...,m]\n";
+                 "[--check-tasks] [--engine tasks|mlp] [--dtype tf32|bf16] [--bias] [--layers n,...,m] "
+                 "[--repeats R] [--perf] [--perf-json PATH] [--print-profile] [--seg-window W]\n";
     return 2;
   }
   std::cout << "Megakernel Training Demo (B200)\n========================\n";

@@ -10,6 +10,9 @@
 #ifndef __device__
 #define __device__
 #endif
+#ifndef __host__
+#define __host__
+#endif
 #endif
 
 namespace pk {
@@ -48,12 +51,12 @@ struct WarpRoles {
 __device__ inline int lane_id() { return threadIdx.x & (Config::kWarpSize - 1); }
 __device__ inline int warp_id() { return threadIdx.x / Config::kWarpSize; }
 #endif
-__device__ inline bool is_controller(int wid, const WarpRoles& r) { return wid == r.controller; }
-__device__ inline bool is_loader(int wid, const WarpRoles& r) { return wid == r.loader; }
-__device__ inline bool is_storer(int wid, const WarpRoles& r) { return wid == r.storer; }
-__device__ inline bool is_compute(int wid, const WarpRoles& r) {
+__host__ __device__ inline bool is_controller(int wid, const WarpRoles& r) { return wid == r.controller; }
+__host__ __device__ inline bool is_loader(int wid, const WarpRoles& r) { return wid == r.loader; }
+__host__ __device__ inline bool is_storer(int wid, const WarpRoles& r) { return wid == r.storer; }
+__host__ __device__ inline bool is_compute(int wid, const WarpRoles& r) {
   return wid >= r.first_compute && wid < r.first_compute + r.num_compute;
 }
-__device__ inline int compute_warp_index(int wid, const WarpRoles& r) { return wid - r.first_compute; }
+__host__ __device__ inline int compute_warp_index(int wid, const WarpRoles& r) { return wid - r.first_compute; }
 
 }  // namespace pk

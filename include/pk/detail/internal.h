@@ -4,7 +4,7 @@
 #include <cuda.h>
 #include <cstdint>
 
-#include "../../include/pkt_b200.h"
+#include "../../pkt_b200.h"
 
 namespace pkb {
 

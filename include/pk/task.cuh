@@ -48,7 +48,7 @@ static_assert(sizeof(Task) == 96 && alignof(Task) == 16, "Task is 96 bytes, 16-a
 static_assert(sizeof(Task) == sizeof(pkt_task), "pk::Task matches the C-ABI descriptor");
 
 template <typename Args>
-inline const Args& decode_args(const Task& t) {
+__host__ __device__ inline const Args& decode_args(const Task& t) {
   static_assert(std::is_trivially_copyable_v<Args>, "Args must be trivially copyable");
   static_assert(sizeof(Args) <= Config::kArgBytes, "Args size exceeds task payload capacity");
   return *reinterpret_cast<const Args*>(t.args);

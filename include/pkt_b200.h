@@ -227,6 +227,14 @@ int pkt_runtime_set_perf(pkt_runtime* rt, int enabled);
 #define PKT_PERF_WORDS 16
 int pkt_runtime_fetch_perf(pkt_runtime* rt, unsigned long long* out, int max_blocks, int* blocks);
 int pkt_runtime_last_launch_blocks(pkt_runtime* rt);
+/* For launching the megakernel instantiated with a program's own pk::OpTraits ops
+ * (pk/kernel.cuh, pk::launch_with_ops; no counterpart in pkt, whose ops are
+ * compiled into its one kernel): prepares the submitted list exactly as
+ * pkt_runtime_launch does (grid clamped to the resident CTAs, counters cleared on
+ * `stream`) and returns the kernel's parameter block (kparams_bytes must equal the
+ * caller's sizeof(pkb::KParams)), the grid and the CTA-pair mode. */
+int pkt_runtime_prepare_launch(pkt_runtime* rt, int num_blocks, void* stream, void* kparams, int kparams_bytes,
+                               int* blocks, int* pair);
 /* Effective SM clock of the launches since the last reset (no counterpart in pkt):
  * out3 = {SM cycles, nanoseconds, launches} summed over CTA 0's lifetime in every
  * launch; cycles * 1000 / ns is the mean SM clock in MHz. reset != 0 clears the

@@ -71,6 +71,50 @@ int pktref_axpy(const float* hx, float* hy, float a, int num_tasks, int per_task
   return 0;
 }
 
+// pkt's Axpy launch timed on the device: num_tasks tasks of `per_task` elements
+// over device buffers it allocates (x, y uniform in [-1, 1)); `reps` launches after
+// one untimed, each timed with CUDA events around runtime.launch (the task list is
+// resubmitted before each, outside the timing). *ms receives the fastest launch.
+int pktref_axpy_time(int num_tasks, int per_task, int blocks, int reps, float* ms) {
+  const size_t n = size_t(num_tasks) * per_task;
+  float *dx = nullptr, *dy = nullptr;
+  HCHECK(cudaMalloc(&dx, n * 4));
+  HCHECK(cudaMalloc(&dy, n * 4));
+  HCHECK(cudaMemset(dx, 0, n * 4));
+  HCHECK(cudaMemset(dy, 0, n * 4));
+  cudaEvent_t a, b;
+  HCHECK(cudaEventCreate(&a));
+  HCHECK(cudaEventCreate(&b));
+  float best = -1.f;
+  {
+    pk::Runtime rt;
+    rt.initialize(num_tasks);
+    std::vector<pk::Task> tasks(num_tasks);
+    for (int i = 0; i < num_tasks; ++i) {
+      pk::AxpyArgs args{dx + size_t(i) * per_task, dy + size_t(i) * per_task, 0.5f, per_task};
+      pk::encode_args(tasks[i], pk::OpCode::Axpy, args);
+    }
+    for (int r = 0; r <= reps; ++r) {
+      rt.submit_tasks(tasks);
+      HCHECK(cudaDeviceSynchronize());
+      HCHECK(cudaEventRecord(a));
+      rt.launch(blocks > 0 ? blocks : pk::Runtime::get_num_sms());
+      HCHECK(cudaEventRecord(b));
+      rt.synchronize();
+      float t = 0.f;
+      HCHECK(cudaEventElapsedTime(&t, a, b));
+      if (r > 0 && (best < 0.f || t < best)) best = t;
+    }
+  }
+  HCHECK(cudaGetLastError());
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  cudaFree(dx);
+  cudaFree(dy);
+  *ms = best;
+  return 0;
+}
+
 // pkt's single-Linear training DAG (same task structure as the train_linear
 // example: zero loss, forward tiles, MSE, zero dW, backward tiles, SGD), all
 // steps in one launch, but each step's MSELossArgs.loss points at its own slot

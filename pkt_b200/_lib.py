@@ -84,6 +84,7 @@ _SIGS = {
     "pkt_runtime_fetch_perf": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
     "pkt_runtime_last_launch_blocks": ([_P], c_int),
     "pkt_runtime_clock_stats": ([_P, _P, c_int], c_int),
+    "pkt_runtime_prepare_launch": ([_P, c_int, _P, _P, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int)], c_int),
     "pkt_runtime_set_trace": ([_P, c_int], c_int),
     "pkt_runtime_fetch_trace": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
     "pkt_axpy": ([_P, _P, c_float, c_longlong, _P], c_int),

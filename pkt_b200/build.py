@@ -18,6 +18,9 @@ def needs_build():
     t = os.path.getmtime(OUT)
     deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)]
     deps.append(os.path.join(HERE, "..", "include", "pkt_b200.h"))
+    for sub in ("pk", os.path.join("pk", "detail")):
+        d = os.path.join(HERE, "..", "include", sub)
+        deps += [os.path.join(d, f) for f in os.listdir(d) if f.endswith((".cuh", ".h", ".hpp"))]
     return any(os.path.getmtime(d) > t for d in deps)
 
 

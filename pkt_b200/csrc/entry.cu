@@ -7,7 +7,7 @@
 #include <mutex>
 #include <vector>
 
-#include "internal.h"
+#include "../../include/pk/detail/internal.h"
 #include "runtime_impl.h"
 
 namespace pkb {
@@ -31,8 +31,14 @@ extern "C" int pkt_axpy(const float* x, float* y, float a, long long n, void* st
     if (rc) return rc;
   }
   Runtime* rt = g_axpy_rt[dev];
-  // 32K floats per task: 256 KB of traffic, several tasks per SM for balance.
-  const long long chunk = 32768;
+  // 128K floats per task: 1.5 MB of traffic, so the per-task handoff is a few
+  // per cent of its time, and still several tasks per SM for balance at the
+  // sizes where bandwidth matters; small arrays are split finer so every SM
+  // gets work.
+  long long chunk = 131072;
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  while (chunk > 4096 && (n + chunk - 1) / chunk < 4LL * sms) chunk /= 2;
   const int ntask = int((n + chunk - 1) / chunk);
   std::vector<pkt_task>& tl = g_axpy_tasks[dev];
   tl.assign(ntask, pkt_task{});

@@ -23,7 +23,7 @@
 #include <cstring>
 #include <vector>
 
-#include "internal.h"
+#include "../../include/pk/detail/internal.h"
 #include "runtime_impl.h"
 
 namespace pkb {

@@ -28,7 +28,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "internal.h"
+#include "../../include/pk/detail/internal.h"
 #include "runtime_impl.h"
 
 namespace pkb {

@@ -14,7 +14,7 @@
 #include <string>
 #include <vector>
 
-#include "internal.h"
+#include "../../include/pk/detail/internal.h"
 #include "runtime_impl.h"
 
 namespace pkb {
@@ -393,6 +393,15 @@ int Runtime::reset_state(cudaStream_t stream, bool sync) {
 }
 
 int Runtime::launch(int blocks, cudaStream_t stream) {
+  KParams p{};
+  int rc = prepare(blocks, stream, &p, &blocks);
+  if (rc) return rc;
+  cudaError_t e = launch_megakernel(p, blocks, stream, cta_pair);
+  if (e != cudaSuccess) return cuda_fail(e, "launch megakernel");
+  return PKT_OK;
+}
+
+int Runtime::prepare(int blocks, cudaStream_t stream, KParams* out, int* out_blocks) {
   cudaSetDevice(device);
   if (!d_state) return fail(PKT_ERR_ARGS, "runtime not initialized");
   // pkt launches whatever grid it is given (include/runtime.hpp:175-228); a
@@ -423,8 +432,8 @@ int Runtime::launch(int blocks, cudaStream_t stream) {
   rc = trace_for(num_tasks, stream, &p.trace);
   if (rc) return rc;
   last_blocks = blocks;
-  cudaError_t e = launch_megakernel(p, blocks, stream, cta_pair);
-  if (e != cudaSuccess) return cuda_fail(e, "launch megakernel");
+  *out = p;
+  *out_blocks = blocks;
   return PKT_OK;
 }
 
@@ -649,6 +658,18 @@ int pkt_runtime_set_trace(pkt_runtime* rt, int enabled) {
 int pkt_runtime_fetch_trace(pkt_runtime* rt, unsigned long long* out, int max_tasks, int* n) {
   if (!rt || !out || !n) return pkb::fail(PKT_ERR_ARGS, "null argument");
   return rt->rt->fetch_trace(out, max_tasks, n);
+}
+
+int pkt_runtime_prepare_launch(pkt_runtime* rt, int num_blocks, void* stream, void* kparams, int kparams_bytes,
+                               int* blocks, int* pair) {
+  if (!rt || !kparams || !blocks || !pair) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  if (kparams_bytes != int(sizeof(pkb::KParams)))
+    return pkb::fail(PKT_ERR_ARGS, "kernel parameter block is %d bytes here, %d in the caller's headers",
+                     int(sizeof(pkb::KParams)), kparams_bytes);
+  int rc = rt->rt->prepare(num_blocks, static_cast<cudaStream_t>(stream), static_cast<pkb::KParams*>(kparams), blocks);
+  if (rc) return rc;
+  *pair = rt->rt->cta_pair;
+  return PKT_OK;
 }
 
 int pkt_runtime_clock_stats(pkt_runtime* rt, unsigned long long* out3, int reset) {

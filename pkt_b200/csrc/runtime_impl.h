@@ -5,7 +5,7 @@
 
 #include <vector>
 
-#include "internal.h"
+#include "../../include/pk/detail/internal.h"
 
 namespace pkb {
 
@@ -54,6 +54,9 @@ struct Runtime {
   int submit_async(const pkt_task* tasks, int n, cudaStream_t stream, bool sync_copy);
   int reset_state(cudaStream_t stream, bool sync);
   int launch(int blocks, cudaStream_t stream);
+  // Everything launch does but the launch: the grid (clamped), the cleared
+  // counters and the kernel parameters of the submitted list.
+  int prepare(int blocks, cudaStream_t stream, KParams* out, int* out_blocks);
   int status(int* code, int* task, int* detail);
   int register_gemms(const pkt_gemm_desc* descs, int n, int* first);
   // Clamps a persistent grid to the CTAs that fit on the device at once (and to

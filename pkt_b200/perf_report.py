@@ -3,6 +3,7 @@
     python -m pkt_b200.perf_report --dims 1024,4096,4096,4096,1024 --batch 8192
     python -m torch.distributed.run --nproc-per-node 8 -m pkt_b200.perf_report --grad-mode 2
     python -m pkt_b200.perf_report --axpy 268435456
+    python -m pkt_b200.perf_report --sgd 268435456
 
 Times `--steps` steps with CUDA events, then runs one more step with the
 per-CTA counters on and prints, for the leader CTA of every CTA pair, the mean
@@ -16,7 +17,8 @@ between the backward and the update launch; every rank prints its step time and
 rank 0 its counters.
 
 --axpy N instead times pkt_axpy (y = a*x + y over N floats already on the device,
-12 bytes per element: read x, read y, write y) and prints its HBM bandwidth.
+12 bytes per element: read x, read y, write y) and prints its HBM bandwidth;
+--sgd N the SGDMixed update pass over N parameters (14 bytes per parameter).
 """
 import argparse
 import os
@@ -58,6 +60,47 @@ def axpy_report(args):
           f"{12.0 * n / ms / 1e6:.0f} GB/s (12 B per element)")
 
 
+def sgd_report(args):
+    """SGDMixed tasks (fp32 master w -= lr * g in place, bf16 copy of the new w
+    written alongside: 14 bytes per parameter -- read w, read g, write w, write
+    the copy) over N parameters already on the device, in chunks of 2^20 per task,
+    one persistent launch per pass (the grad_mode 1 update pass of the MLP engine)."""
+    import torch
+    import pkt_b200
+    from pkt_b200 import runtime as R
+
+    n = args.sgd
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    w = torch.rand(n, device="cuda")
+    g = torch.rand(n, device="cuda") * 1e-3
+    wb = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    chunk = 1 << 20
+    ntask = (n + chunk - 1) // chunk
+    tasks = R.make_tasks(ntask)
+    for i in range(ntask):
+        k = min(chunk, n - i * chunk)
+        a = R.SGDMixedArgs(w.data_ptr() + 4 * i * chunk, g.data_ptr() + 4 * i * chunk, w.data_ptr() + 4 * i * chunk,
+                           wb.data_ptr() + 2 * i * chunk, k, 1e-3, 0)
+        R.encode_args(tasks[i], R.OpCode.SGDMixed, a)
+    rt = pkt_b200.Runtime()
+    rt.initialize(ntask)
+    per = []
+    for it in range(args.warmup + args.steps):
+        rt.submit_tasks(tasks)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        rt.launch(0)
+        e1.record()
+        rt.synchronize()
+        if it >= args.warmup:
+            per.append(e0.elapsed_time(e1))
+    per.sort()
+    ms = per[len(per) // 2]
+    print(f"sgd_mixed n={n}: {ms:.3f} ms per pass (median of {args.steps}), "
+          f"{14.0 * n / ms / 1e6:.0f} GB/s (14 B per parameter)")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--dims", default="1024,4096,4096,4096,1024")
@@ -70,9 +113,13 @@ def main(argv=None):
                          "2: fused peer-memory reduce (default with WORLD_SIZE > 1)")
     ap.add_argument("--axpy", type=int, default=0, metavar="N",
                     help="time pkt_axpy over N floats instead of an MLP step")
+    ap.add_argument("--sgd", type=int, default=0, metavar="N",
+                    help="time the SGDMixed update pass over N parameters instead of an MLP step")
     args = ap.parse_args(argv)
     if args.axpy:
         return axpy_report(args)
+    if args.sgd:
+        return sgd_report(args)
 
     import torch
     import pkt_b200

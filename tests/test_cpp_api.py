@@ -76,3 +76,18 @@ def test_train_linear_example_mlp_layers_bf16():
     first = float(re.search(r"Device first step loss: ([0-9.e+-]+)", out).group(1))
     last = float(re.search(r"Device final loss: ([0-9.e+-]+)", out).group(1))
     assert last < first, out
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("engine", ["tasks", "mlp"])
+def test_train_linear_perf_json(engine, tmp_path):
+    """--perf / --perf-json (pkt examples/train_linear.cu:724-935): per-role summary
+    printed, JSON written with the per-CTA totals."""
+    import json
+    path = str(tmp_path / "perf.json")
+    rc, out = _run(_make("train_linear"), "--m", "256", "--n", "512", "--batch", "64", "--steps", "8",
+                   "--lr", "0.01", "--skip-cpu", "--engine", engine, "--perf-json", path)
+    assert rc == 0, out
+    assert "Per-role counters" in out and "controller.deps_wait" in out, out
+    d = json.load(open(path))
+    assert d["blocks"] > 0 and d["totals"]["tasks_issued"] > 0 and d["sm_mhz"] > 0
