@@ -153,7 +153,14 @@ def cpu_full_batch(cfg, max_steps, budget_s, warmup=1):
     `budget_s` seconds. Returns (result dict, description)."""
     from oracle import cpu_baseline as cb
     x, t, Ws, bs = make_inputs(cfg, 0)
-    r = cb.time_mlp(cfg["dims"], x, t, Ws, bs, cfg["lr"], max_steps, budget_s, warmup=warmup)
+    # every host CPU this process may run on (torchrun sets OMP_NUM_THREADS=1 for
+    # its ranks; the baseline overrides it)
+    try:
+        threads = len(os.sched_getaffinity(0))
+    except AttributeError:
+        threads = os.cpu_count() or 1
+    r = cb.time_mlp(cfg["dims"], x, t, Ws, bs, cfg["lr"], max_steps, budget_s, warmup=warmup,
+                    threads=threads)
     desc = (f"{r['steps']} full-batch step(s) of {cfg['batch']} rows timed ({r['seconds']:.2f} s) "
             f"after {warmup} untimed; fp32 OpenMP restatement of pkt's host loop extended to the MLP "
             f"({cb.FLAGS}), {r['threads']} threads on {os.cpu_count()} logical CPUs, {cb.cpu_model()}")
