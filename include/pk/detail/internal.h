@@ -109,7 +109,6 @@ struct alignas(128) DevGemm {
   CUtensorMap map_pf;      // the matrix the epilogue reads rows of (aux or w_in): L2 prefetch boxes
   int pf_ok;               // 1: map_pf is valid (the loader prefetches each tile's box)
   int pad_pf;
-  CUtensorMap map_peer[PKT_DP_MAX_RANKS];  // WGRAD_PEER owner: w_shadow's twin on every rank
 };
 
 // Per-CTA perf words (pkt_runtime_fetch_perf), cycles unless noted.

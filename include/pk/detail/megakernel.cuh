@@ -67,7 +67,7 @@ struct SmemT {
   uint64_t mma_drain;
   uint64_t pair_done[kSlots];  // leader: the other CTA of the pair finished task seq
   uint32_t tmem_base;
-  int dp_ok;  // WGRAD_PEER owner: the other ranks' partials of the current tile arrived
+  int dp_ok;  // PKT_OP_DP_REDUCE: every rank's partial of the current tile arrived
   pk::PipelineSlot user_slot;                  // the task a pk::OpTraits op sees as br.slot(0)
   pk::PageMeta page_meta[pk::Config::kPagesPerSlot];  // leases / tags of its pages (in epi_stage)
   float red[8][4][32];  // per 32-column chunk, per TMEM lane quadrant: column partial sums
@@ -135,7 +135,7 @@ __device__ __forceinline__ bool opcode_known(uint16_t op) {
          op == PKT_OP_GEMM || op == PKT_OP_LINEAR_FORWARD || op == PKT_OP_MSE_LOSS ||
          op == PKT_OP_LINEAR_BACKWARD || op == PKT_OP_SGD_UPDATE || op == PKT_OP_BIAS_SGD ||
          op == PKT_OP_LOSS_REDUCE || op == PKT_OP_SGD_MIXED || op == PKT_OP_DP_WAIT ||
-         op == PKT_OP_DP_BIAS_SEND || op == PKT_OP_DP_BIAS_APPLY;
+         op == PKT_OP_DP_BIAS_SEND || op == PKT_OP_DP_BIAS_APPLY || op == PKT_OP_DP_REDUCE;
 }
 
 __device__ __forceinline__ void copy_task(pkt_task* dst, const pkt_task* src) {
@@ -729,44 +729,21 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
   const bool tma_out = g.tma_out != 0, tma_w = g.tma_w != 0;
   uint8_t* const stg = s.epi_stage[c.q];
   const int row0 = rblock * kBM + c.q * 32;
-  // WGRAD_PEER (fused data parallel): tile t belongs to rank t % world. A
-  // non-owner writes its fp32 partial rows into its slot in the owner's
-  // exchange region; the owner waits for the other ranks' slots, sums the
-  // partials in rank order (its own from TMEM), applies SGD to the master and
-  // writes the new bf16 rows into every rank's copy. Slot rows are 256 floats.
+  // WGRAD_PEER (fused data parallel): tile t belongs to rank t % world. Every
+  // rank, the owner included, writes its fp32 partial rows into its own slot of
+  // the tile in the owner's exchange region and counts one arrival there; the
+  // owner's PKT_OP_DP_REDUCE task, listed later, sums the slots. No epilogue waits
+  // on another rank. Slot rows are 256 floats.
   const DpPeers* dp = epi == PKT_EPI_WGRAD_PEER ? p.dp : nullptr;
   if (epi == PKT_EPI_WGRAD_PEER && dp == nullptr) set_error(p, PKT_DEV_BAD_ARGS, -1, -3);
   const int dp_t = g.dp_tile_base + tile_m * g.tiles_n + tile_n;
-  const bool dp_owner = dp != nullptr && dp_t % dp->world == dp->rank;
   const int dp_tl = dp != nullptr ? dp_t / dp->world : 0;
-  const int slot_row = int(c.rank) * kBM + c.q * 32 + c.lane;
-  int peer_slot_row0 = 0;      // non-owner: the warp's first row in the owner's slot matrix
-  int* peer_arrive = nullptr;  // non-owner: the owner's arrival counter of this tile
-  const float* own_slots = nullptr;  // owner: slot 0 of this tile, this thread's row
-  long long shadow_off = 0;          // owner: byte offset of the bf16 copy in a region
-  bool dp_skip = false;              // owner whose wait for the partials failed
+  int peer_slot_row0 = 0;      // the warp's first row in the owner's slot matrix
+  int* peer_arrive = nullptr;  // the owner's arrival counter of this tile
   if (dp != nullptr) {
-    const int owner = dp_t % dp->world;
-    uint8_t* ob = dp->base[owner];
-    const float* slots0 = reinterpret_cast<const float*>(ob + dp->recv_off + (long long)dp_tl * dp->world * dp->slot_bytes);
-    if (!dp_owner) {
-      peer_slot_row0 = int(((long long)dp_tl * dp->world + dp->rank) * dp->pair * kBM) + int(c.rank) * kBM + c.q * 32;
-      peer_arrive = reinterpret_cast<int*>(ob + dp->arrive_off) + dp_tl;
-    } else {
-      own_slots = slots0 + (long long)slot_row * 256;
-      shadow_off = reinterpret_cast<const uint8_t*>(w_shadow) - dp->base[dp->rank];
-      if (c.et == 0)
-        s.dp_ok = dp->world > 1
-                      ? int(dp_wait_geq(p, reinterpret_cast<const int*>(ob + dp->arrive_off) + dp_tl,
-                                        (p.dp_step + 1) * (dp->world - 1) * dp->pair, 4000 + g.dp_layer))
-                      : 1;
-      epi_sync();
-      // A wait that ran out (the status word is set) leaves this tile's master
-      // shard and every rank's weight copy as they were: partial slots that are
-      // stale or half-written are never summed, nothing is broadcast and no
-      // arrival is counted, so the step fails without corrupting the weights.
-      dp_skip = s.dp_ok == 0;
-    }
+    uint8_t* ob = dp->base[dp_t % dp->world];
+    peer_slot_row0 = int(((long long)dp_tl * dp->world + dp->rank) * dp->pair * kBM) + int(c.rank) * kBM + c.q * 32;
+    peer_arrive = reinterpret_cast<int*>(ob + dp->arrive_off) + dp_tl;
   }
   // bf16 output chunks are 2 KB: three of them rotate through the warp's 6 KB
   // staging area, so a chunk is staged while the two before it are still being
@@ -909,7 +886,7 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = (j < nvalid && h[j] > 0.f) ? v[j] : 0.f;
       emit_out(v, col0, nvalid);
-    } else if (epi == PKT_EPI_WGRAD_PEER && !dp_owner) {
+    } else if (epi == PKT_EPI_WGRAD_PEER) {
       // the warp's 32 x 32 fp32 chunk goes to the owner as one TMA tile store
       if (dp != nullptr) {
         if (c.lane == 0) bulk_wait_read_all();
@@ -922,33 +899,7 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
           bulk_commit();
         }
       }
-    } else if (dp_skip) {
-      // owner after a failed wait: the accumulator is only drained
-    } else if (epi == PKT_EPI_WGRAD_SGD || dp_owner) {
-      if (dp_owner) {
-        // rank-ordered sum of the partials; this rank's own is v
-        float gsum[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) gsum[j] = 0.f;
-        for (int src = 0; src < dp->world; ++src) {
-          if (src == dp->rank) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) gsum[j] += v[j];
-          } else {
-            const float4* pr = reinterpret_cast<const float4*>(own_slots + src * (dp->slot_bytes / 4) + ch * 32);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float4 q4 = __ldcg(pr + i);
-              gsum[4 * i] += q4.x;
-              gsum[4 * i + 1] += q4.y;
-              gsum[4 * i + 2] += q4.z;
-              gsum[4 * i + 3] += q4.w;
-            }
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gsum[j];
-      }
+    } else if (epi == PKT_EPI_WGRAD_SGD) {
       float w[32];
       const long long ow = (long long)row * ldw + col0;
       const bool wvec = aligned16(w_in + ow) && aligned16(w_out + ow);
@@ -970,9 +921,6 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
         if (c.lane == 0 && row0 < M && col0 < N) {
           tma_store_2d(&g.map_w, stg, col0, row0);
           if (w_shadow) tma_store_2d(&g.map_shadow, stg + 4096, col0, row0);
-          if (dp_owner)  // the new bf16 chunk into the other ranks' copies
-            for (int r2 = 0; r2 < dp->world; ++r2)
-              if (r2 != dp->rank) tma_store_2d(&g.map_peer[r2], stg + 4096, col0, row0);
           bulk_commit();
         }
       } else if (nvalid > 0) {
@@ -986,25 +934,6 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
         if (w_shadow) {
           const bool svec = aligned16(reinterpret_cast<const uint16_t*>(w_shadow) + ow);
           store_row32(w_shadow, PKT_DTYPE_BF16, ow, nvalid, svec, w2);
-        }
-      }
-      if (dp_owner && !tma_w && nvalid > 0) {
-        // the new bf16 row into the other ranks' copies (w holds the new master,
-        // possibly already rounded to bf16: rounding again changes nothing)
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(w[2 * i], w[2 * i + 1]);
-        for (int r2 = 0; r2 < dp->world; ++r2) {
-          if (r2 == dp->rank) continue;
-          uint16_t* dst = reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + ow;
-          if (nvalid == 32 && aligned16(dst)) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-          } else {
-            for (int j = 0; j < nvalid; ++j)
-              dst[j] = uint16_t((j & 1) ? (pk[j >> 1] >> 16) : (pk[j >> 1] & 0xffffu));
-          }
         }
       }
     }
@@ -1054,18 +983,11 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
   __syncwarp();
   if (dp != nullptr) {
     // every thread's rows (TMA stores included) visible system-wide, then one
-    // arrive per CTA: a non-owner on the owner's counter of this tile, the
-    // owner on every rank's counter of the layer's next-step weights
+    // arrive per CTA on the owner's counter of this tile
     fence_proxy_async_global();
     __threadfence_system();
     epi_sync();
-    if (c.et == 0) {
-      if (!dp_owner)
-        red_release_sys_add(peer_arrive, 1);
-      else if (!dp_skip)
-        for (int r2 = 0; r2 < dp->world; ++r2)
-          red_release_sys_add(reinterpret_cast<int*>(dp->base[r2] + dp->wready_off) + g.dp_layer, 1);
-    }
+    if (c.et == 0) red_release_sys_add(peer_arrive, 1);
   }
 }
 
@@ -1288,6 +1210,78 @@ __device__ void op_dp_wait(const KParams& p, const EpiCtx& c, const pkt_dp_wait_
   epi_sync();
 }
 
+// An owned weight tile of the step (fused data parallel): once every rank's
+// partial of the tile has arrived in this rank's slots (its arrival counter,
+// one count per rank and CTA of a pair), the partials are summed in rank order,
+// SGD updates the fp32 master (this rank owns it) and the new bf16 values go to
+// every rank's copy of the next step's weights, own included; then every rank's
+// "layer weights arrived" counter gets one count per CTA. A wait that runs out
+// (the status word is set) leaves the master and every copy as they were and
+// counts nothing, so the step fails without corrupting the weights.
+template <int P>
+__device__ void op_dp_reduce(const KParams& p, SmemT<P>& s, const EpiCtx& c, const pkt_gemm_tile_args& a) {
+  const DpPeers* dp = p.dp;
+  if (dp == nullptr || int(a.gemm) >= p.num_gemms) return;
+  const DevGemm& g = p.gemms[a.gemm];
+  const pkt_gemm_desc& d = g.d;
+  const int t = g.dp_tile_base + int(a.tile_m) * g.tiles_n + int(a.tile_n);
+  const int tl = t / dp->world;
+  uint8_t* own = dp->base[dp->rank];
+  if (c.et == 0)
+    s.dp_ok = int(dp_wait_geq(p, reinterpret_cast<const int*>(own + dp->arrive_off) + tl,
+                              (p.dp_step + 1) * dp->world * dp->pair, 4000 + g.dp_layer));
+  epi_sync();
+  const bool ok = s.dp_ok != 0;
+  epi_sync();  // every thread has read the flag before the next task may rewrite it
+  if (!ok) return;
+  const int rows_tile = dp->pair * kBM;
+  const int row0 = int(a.tile_m) * rows_tile, n0 = int(a.tile_n) * d.bn;
+  const int rows = min(rows_tile, d.M - row0), cols = min(d.bn, d.N - n0);
+  const float* slots = reinterpret_cast<const float*>(own + dp->recv_off + (long long)tl * dp->world * dp->slot_bytes);
+  const long long slot_floats = dp->slot_bytes / 4;
+  const long long shadow_off = reinterpret_cast<const uint8_t*>(d.w_shadow) - own;
+  const float lr = d.lr;
+  const long long ldw = d.ldw;
+  const int cg = (cols + 3) / 4;  // groups of 4 columns per row
+  for (long long e = c.tid; e < (long long)rows * cg; e += c.nthr) {
+    const int r = int(e / cg), c4 = int(e % cg) * 4;
+    const int nv = min(4, cols - c4);
+    float gs[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int src = 0; src < dp->world; ++src) {
+      const float* sp = slots + src * slot_floats + (long long)r * 256 + c4;
+      if (nv == 4) {
+        const float4 q = __ldcg(reinterpret_cast<const float4*>(sp));
+        gs[0] += q.x;
+        gs[1] += q.y;
+        gs[2] += q.z;
+        gs[3] += q.w;
+      } else {
+        for (int k = 0; k < nv; ++k) gs[k] += __ldcg(sp + k);
+      }
+    }
+    const long long idx = (long long)(row0 + r) * ldw + n0 + c4;
+    float w[4];
+    for (int k = 0; k < nv; ++k) w[k] = fmaf(-lr, gs[k], d.w_in[idx + k]);
+    for (int k = 0; k < nv; ++k) d.w_out[idx + k] = w[k];
+    if (nv == 4 && (idx & 3) == 0) {
+      const uint2 pk = make_uint2(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]));
+      for (int r2 = 0; r2 < dp->world; ++r2)
+        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + idx) = pk;
+    } else {
+      for (int k = 0; k < nv; ++k) {
+        const uint16_t h = f32_to_bf16_rn(w[k]);
+        for (int r2 = 0; r2 < dp->world; ++r2)
+          reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off)[idx + k] = h;
+      }
+    }
+  }
+  __threadfence_system();
+  epi_sync();
+  if (c.et == 0)
+    for (int r2 = 0; r2 < dp->world; ++r2)
+      red_release_sys_add(reinterpret_cast<int*>(dp->base[r2] + dp->wready_off) + g.dp_layer, 1);
+}
+
 // This rank's bias gradient of one layer (column partials summed in row-block
 // order) into every rank's receive vector for this step's parity.
 __device__ void op_dp_bias_send(const KParams& p, const EpiCtx& c, const pkt_dp_bias_args& a) {
@@ -1441,6 +1435,9 @@ __device__ void compute_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base, 
         break;
       case PKT_OP_DP_BIAS_SEND:
         op_dp_bias_send(p, c, *reinterpret_cast<const pkt_dp_bias_args*>(task.args));
+        break;
+      case PKT_OP_DP_REDUCE:
+        op_dp_reduce<P>(p, s, c, *reinterpret_cast<const pkt_gemm_tile_args*>(task.args));
         break;
       case PKT_OP_DP_BIAS_APPLY:
         op_dp_bias_apply(p, c, *reinterpret_cast<const pkt_dp_bias_args*>(task.args));

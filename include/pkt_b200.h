@@ -73,7 +73,9 @@ enum pkt_opcode {
   /* Fused data parallel (MLP grad_mode 2; peer memory between the ranks' GPUs): */
   PKT_OP_DP_WAIT = 30,        /* pkt_dp_wait_args: the next step's weights of a layer have arrived */
   PKT_OP_DP_BIAS_SEND = 31,   /* pkt_dp_bias_args: this rank's bias gradient to every rank */
-  PKT_OP_DP_BIAS_APPLY = 32   /* pkt_dp_bias_args: sum the ranks' bias gradients, SGD */
+  PKT_OP_DP_BIAS_APPLY = 32,  /* pkt_dp_bias_args: sum the ranks' bias gradients, SGD */
+  PKT_OP_DP_REDUCE = 33       /* pkt_gemm_tile_args: an owned weight tile: sum the ranks' partials,
+                                 SGD on the fp32 master, new bf16 tile to every rank */
 };
 
 /* Args of PKT_OP_GEMM: tile (tile_m, tile_n) of registered GEMM `gemm`. */

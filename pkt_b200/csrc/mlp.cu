@@ -528,10 +528,6 @@ int Mlp::build(int p, int q) {
         return fail(PKT_ERR_UNSUPPORTED, "weight tile layout differs from the exchange region's");
       dg.dp_tile_base = wg_base[l];
       dg.dp_layer = l;
-      for (int r = 0; r < dp_world; ++r)
-        if (!make_store_map(&dg.map_peer[r], hdp.base[r] + wbf_off[nxt][l], PKT_DTYPE_BF16, dims[l],
-                            dims[l + 1], ld[l]))
-          return fail(PKT_ERR_CUDA, "tensor map over rank %d's weight copy", r);
       cudaError_t e = cudaMemcpy(rt->d_gemms + first + wgr[l], &dg, sizeof(DevGemm), cudaMemcpyHostToDevice);
       if (e != cudaSuccess) return cuda_fail(e, "copy gemm table");
     }
@@ -703,9 +699,15 @@ int Mlp::build(int p, int q) {
   } else {
     // Fused data parallel: each layer's weight-gradient tiles follow its dgrad
     // tiles, so partial tiles cross to their owners (and the owners' new
-    // weights back) while the rest of the backward runs.
+    // weights back) while the rest of the backward runs. A weight-gradient
+    // epilogue only sends its partial; the owner's reduce task of a tile (sum,
+    // SGD, new bf16 tile to every rank) is listed in the next layer's dgrad block,
+    // after two waves of it (layer 0's last): by then every rank has normally
+    // sent its partial, so the reduce rarely waits, and no GEMM epilogue ever
+    // waits on another rank.
     const float lre = lr * grad_scale;
-    std::vector<pkt_task> deferred;  // this rank's own weight tiles of the previous layer
+    std::vector<pkt_task> deferred;  // this rank's reduce tasks of the previous layer
+    std::vector<pkt_task> last;      // layer 0's reduce tasks
     for (int l = L - 1; l >= 0; --l) {
       if (l >= 1) {
         const DevGemm& dg = G(dgr[l]);
@@ -718,8 +720,6 @@ int Mlp::build(int p, int q) {
             t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
             tl.push_back(t);
             ++tiles;
-            // this rank's own weight tiles of layer l+1 go in after two waves of
-            // these dgrad tiles
             if (!deferred.empty() && (i * dg.tiles_n + j + 1) == 2 * std::max(1, rt->num_sms / P)) {
               for (auto& d2 : deferred) tl.push_back(d2);
               deferred.clear();
@@ -728,16 +728,11 @@ int Mlp::build(int p, int q) {
         for (auto& d2 : deferred) tl.push_back(d2);
         deferred.clear();
       }
-      if (l == 0) { for (auto& d2 : deferred) tl.push_back(d2); deferred.clear(); }
-      // Tiles grouped by owner rank; this rank's own group (whose epilogues wait
-      // for the other ranks' partials) is deferred into the next layer's dgrad
-      // block (wgrad(0)'s stays last): every other rank visits that group
-      // earlier in its own order, so the partials have normally arrived when
-      // the owner gets there, and every wait points at a tile earlier in the
-      // peer's list.
+      // weight-gradient tiles grouped by owner, starting with the next rank's
+      // (this rank's own last): the ranks' partials of a tile leave at different
+      // times, so the owners' slots fill evenly
       const DevGemm& wg = G(wgr[l]);
       const int world = dp_world > 0 ? dp_world : 1, me = dp_world > 0 ? dp_rank : 0;
-      std::vector<pkt_task> own_now;
       for (int k = 1; k <= world; ++k) {
         const int owner = (me + k) % world;
         for (int i = 0; i < wg.tiles_m; ++i)
@@ -746,8 +741,13 @@ int Mlp::build(int p, int q) {
             pkt_task t = gemm_task(wgr[l], i, j);
             t.header.buffer_read_id = uint16_t(BF[l]);
             t.header.wait_count = uint32_t(TM * dy_tn[l]);
-            if (owner == me && l >= 1 && world > 1) deferred.push_back(t); else tl.push_back(t);
+            tl.push_back(t);
             ++tiles;
+            if (owner == me) {
+              pkt_task r = gemm_task(wgr[l], i, j);
+              r.header.opcode = PKT_OP_DP_REDUCE;
+              (l >= 1 ? deferred : last).push_back(r);
+            }
           }
       }
       if (has_bias) {
@@ -767,6 +767,7 @@ int Mlp::build(int p, int q) {
         tl.push_back(t);
       }
     }
+    for (auto& r : last) tl.push_back(r);
     if (has_bias) {
       for (int l = L - 1; l >= 0; --l) {
         pkt_task t{};

@@ -233,7 +233,7 @@ int build_dev_gemm(const pkt_gemm_desc& d, DevGemm* g) {
   if (d.epilogue == PKT_EPI_MSE || d.epilogue == PKT_EPI_DGRAD_RELU)
     g->pf_ok = make_prefetch_map(&g->map_pf, d.aux, d.in_dtype == PKT_DTYPE_BF16 ? PKT_DTYPE_BF16 : PKT_DTYPE_F32,
                                  d.N, d.M, d.ldaux, d.bn);
-  else if (d.epilogue == PKT_EPI_WGRAD_SGD || d.epilogue == PKT_EPI_WGRAD_PEER)
+  else if (d.epilogue == PKT_EPI_WGRAD_SGD)
     g->pf_ok = make_prefetch_map(&g->map_pf, d.w_in, PKT_DTYPE_F32, d.N, d.M, d.ldw, d.bn);
   return PKT_OK;
 }
