@@ -727,6 +727,10 @@ int Mlp::build(int p, int q) {
           }
         for (auto& d2 : deferred) tl.push_back(d2);
         deferred.clear();
+      } else {
+        // layer 0 has no dgrad block: layer 1's reduce tasks go right here
+        for (auto& d2 : deferred) tl.push_back(d2);
+        deferred.clear();
       }
       // weight-gradient tiles grouped by owner, starting with the next rank's
       // (this rank's own last): the ranks' partials of a tile leave at different
