@@ -33,11 +33,16 @@ CONFIGS = {
                       "fp32 accumulate, fp32 master weights, batch 8192/GPU, MSE, SGD lr=1e-3"),
     "cfg3": dict(dims=[512] * 17, batch=2048, dtype="bf16", lr=1e-3,
                  desc="deep narrow MLP: 16 layers of width 512, ReLU, bf16/fp32-acc, batch 2048"),
-    "cfg4": dict(dims=[8192] * 9, batch=8192, dtype="bf16", lr=1e-4,
-                 desc="wide MLP: 8 layers of width 8192, ReLU, bf16/fp32-acc, batch 8192/GPU"),
+    "cfg4": dict(dims=[8192] * 9, batch=8192, dtype="bf16", lr=1e-4, global_batch=65536,
+                 desc="wide MLP: 8 layers of width 8192, ReLU, bf16/fp32-acc, batch 8192/GPU "
+                      "(--scaling strong: global batch 65536 split over the GPUs)"),
     "cfg5": dict(dims=[1000, 3000, 777, 10], batch=4099, dtype="tf32", lr=5e-3,
                  desc="ragged MLP 1000->3000->777->10, fp32 storage with TF32 tensor cores, batch 4099"),
 }
+
+
+for _name, _cfg in CONFIGS.items():
+    _cfg["name"] = _name
 
 
 def flops_per_sample(dims):
@@ -125,7 +130,7 @@ class ClockSampler:
 
 def make_inputs(cfg, rank, seed=1234):
     dims, B = cfg["dims"], cfg["batch"]
-    if cfg is CONFIGS["cfg1"]:
+    if cfg["name"] == "cfg1":
         # train_linear's own recipe: mt19937(0), W ~ U(+-1/sqrt(in)), b = 0, targets
         # from a fixed W*, b* ~ N(0, 1) plus N(0, 0.01^2) noise
         from pkt_b200.data import make_linear_task
@@ -133,7 +138,7 @@ def make_inputs(cfg, rank, seed=1234):
         return x, t, [W], [b]
     rng = np.random.default_rng(seed + rank)
     x = rng.standard_normal((B, dims[0]), dtype=np.float32)
-    if cfg is CONFIGS["cfg5"]:
+    if cfg["name"] == "cfg5":
         x = rng.uniform(-3, 3, (B, dims[0])).astype(np.float32)
         t = np.zeros((B, dims[-1]), np.float32)
         t[np.arange(B), rng.integers(0, dims[-1], B)] = 1.0
@@ -186,7 +191,7 @@ def run_reference(args, cfg_name, cfg):
         "value": v, "unit": "samples/s", "n_gpus": args.gpus, "steps": r["steps"],
         "steps_requested": args.steps, "warmup": min(args.warmup, 1),
         "ms_per_step": 1000.0 * cfg["batch"] / v,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (the same seeded inputs and weights as the GPU arm)",
         "config": {"workload": cfg_name + ": " + cfg["desc"], "global_batch": cfg["batch"],
                    "parallelism": "host CPU, OpenMP"},
@@ -418,7 +423,7 @@ def run_ours(args, cfg_name, cfg):
         "metric": "MLP train samples/s & % dense BF16 TC peak at 1/2/4/8 B200",
         "value": value, "unit": "samples/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"],
+        "scaling": args.scaling, "vs_baseline": None, "dtype": cfg["dtype"],
         "data": "synthetic (seeded N(0,1) inputs/targets, Kaiming-uniform weights, zero bias)",
         "config": {"workload": cfg_name + ": " + cfg["desc"], "global_batch": B * ws,
                    "per_gpu_batch": B,
@@ -473,8 +478,17 @@ def main():
     ap.add_argument("--dp", default="fused", choices=["fused", "nccl"],
                     help="N>1: weight gradients reduced inside the step launch over peer memory "
                          "(fused) or by an NCCL all-reduce between two launches (nccl)")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: the configuration's batch on every GPU; strong: its global batch "
+                         "(cfg4: 65536) split evenly over the GPUs")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
+    if args.scaling == "strong":
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        gb = cfg.get("global_batch", cfg["batch"])
+        if gb % ws:
+            sys.exit(f"global batch {gb} does not split over {ws} GPUs")
+        cfg = dict(cfg, batch=gb // ws)
     if args.impl == "reference":
         run_reference(args, args.config, cfg)
     else:
