@@ -1004,7 +1004,23 @@ __device__ void op_axpy(const AxpyArgs& a, int et, int nthr) {
     // 16 float4 of x and of y in flight per thread (64 KB per 128 threads): the
     // latency of HBM needs that many bytes outstanding per SM to reach its bandwidth
     constexpr int U = 16;
+    // Thread 0 of the task's threads asks the TMA unit to bring the window two
+    // iterations ahead into L2 (each iteration of all threads covers one
+    // contiguous window of U * nthr float4): HBM then sees the bulk engine's
+    // parallelism, and the threads' loads mostly hit L2.
+    const long long win = (long long)U * nthr;
+    auto prefetch = [&](long long w0) {
+      if (w0 >= n4) return;
+      const uint32_t bytes = uint32_t(min(win, n4 - w0) * 16);
+      prefetch_l2_bulk(x4 + w0, bytes);
+      prefetch_l2_bulk(y4 + w0, bytes);
+    };
+    if (et == 0) {
+      prefetch(0);
+      prefetch(win);
+    }
     for (; i + (U - 1) * nthr < n4; i += U * nthr) {
+      if (et == 0) prefetch(i + 2 * win);
       float4 xv[U], yv[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -1062,7 +1078,20 @@ __device__ void op_sgd(const float* W, const float* dW, float* Wo, float lr, lon
     long long i = et;
     // 12 float4 of w and of g in flight per thread (48 KB per 128 threads)
     constexpr int U = 12;
+    // thread 0 brings the window two iterations ahead into L2 (as op_axpy)
+    const long long win = (long long)U * nthr;
+    auto prefetch = [&](long long w0) {
+      if (w0 >= n4) return;
+      const uint32_t bytes = uint32_t(min(win, n4 - w0) * 16);
+      prefetch_l2_bulk(w4 + w0, bytes);
+      prefetch_l2_bulk(g4 + w0, bytes);
+    };
+    if (et == 0) {
+      prefetch(0);
+      prefetch(win);
+    }
     for (; i + (U - 1) * nthr < n4; i += U * nthr) {
+      if (et == 0) prefetch(i + 2 * win);
       float4 w[U], g[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -1243,33 +1272,69 @@ __device__ void op_dp_reduce(const KParams& p, SmemT<P>& s, const EpiCtx& c, con
   const float lr = d.lr;
   const long long ldw = d.ldw;
   const int cg = (cols + 3) / 4;  // groups of 4 columns per row
-  for (long long e = c.tid; e < (long long)rows * cg; e += c.nthr) {
-    const int r = int(e / cg), c4 = int(e % cg) * 4;
-    const int nv = min(4, cols - c4);
-    float gs[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int src = 0; src < dp->world; ++src) {
-      const float* sp = slots + src * slot_floats + (long long)r * 256 + c4;
-      if (nv == 4) {
-        const float4 q = __ldcg(reinterpret_cast<const float4*>(sp));
-        gs[0] += q.x;
-        gs[1] += q.y;
-        gs[2] += q.z;
-        gs[3] += q.w;
-      } else {
-        for (int k = 0; k < nv; ++k) gs[k] += __ldcg(sp + k);
+  const int total = rows * cg;
+  const bool vec = (cols & 3) == 0 && (ldw & 3) == 0 && (n0 & 3) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(d.w_in) | reinterpret_cast<uintptr_t>(d.w_out)) & 15) == 0 &&
+                   (shadow_off & 7) == 0;
+  if (vec) {
+    // U groups of 4 columns per thread and pass, every load of a pass issued
+    // before any of them is used: the slots and the master are read with U x
+    // (world + 1) 16-byte loads in flight per thread instead of one dependent
+    // chain, which is what bounds this pass (it moves ~20 bytes per element).
+    constexpr int U = 8;
+    for (int e0 = c.tid; e0 < total; e0 += U * c.nthr) {
+      float4 gs[U], wv[U];
+      int soff[U];
+      long long idx[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int e = min(e0 + u * c.nthr, total - 1);  // tail: repeats a valid group, stored once
+        const int r = e / cg, c4 = (e - r * cg) * 4;
+        soff[u] = r * 256 + c4;
+        idx[u] = (long long)(row0 + r) * ldw + n0 + c4;
+        gs[u] = __ldcg(reinterpret_cast<const float4*>(slots + soff[u]));
+        wv[u] = *reinterpret_cast<const float4*>(d.w_in + idx[u]);
+      }
+      for (int src = 1; src < dp->world; ++src) {
+        float4 q[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) q[u] = __ldcg(reinterpret_cast<const float4*>(slots + src * slot_floats + soff[u]));
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          gs[u].x += q[u].x;
+          gs[u].y += q[u].y;
+          gs[u].z += q[u].z;
+          gs[u].w += q[u].w;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (e0 + u * c.nthr >= total) break;
+        float4 w;
+        w.x = fmaf(-lr, gs[u].x, wv[u].x);
+        w.y = fmaf(-lr, gs[u].y, wv[u].y);
+        w.z = fmaf(-lr, gs[u].z, wv[u].z);
+        w.w = fmaf(-lr, gs[u].w, wv[u].w);
+        *reinterpret_cast<float4*>(d.w_out + idx[u]) = w;
+        const uint2 pk = make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
+        for (int r2 = 0; r2 < dp->world; ++r2)
+          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + idx[u]) = pk;
       }
     }
-    const long long idx = (long long)(row0 + r) * ldw + n0 + c4;
-    float w[4];
-    for (int k = 0; k < nv; ++k) w[k] = fmaf(-lr, gs[k], d.w_in[idx + k]);
-    for (int k = 0; k < nv; ++k) d.w_out[idx + k] = w[k];
-    if (nv == 4 && (idx & 3) == 0) {
-      const uint2 pk = make_uint2(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]));
-      for (int r2 = 0; r2 < dp->world; ++r2)
-        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + idx) = pk;
-    } else {
+  } else {
+    for (int e = c.tid; e < total; e += c.nthr) {
+      const int r = e / cg, c4 = (e % cg) * 4;
+      const int nv = min(4, cols - c4);
+      float gs[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int src = 0; src < dp->world; ++src) {
+        const float* sp = slots + src * slot_floats + (long long)r * 256 + c4;
+        for (int k = 0; k < nv; ++k) gs[k] = src == 0 ? __ldcg(sp + k) : gs[k] + __ldcg(sp + k);
+      }
+      const long long idx = (long long)(row0 + r) * ldw + n0 + c4;
       for (int k = 0; k < nv; ++k) {
-        const uint16_t h = f32_to_bf16_rn(w[k]);
+        const float w = fmaf(-lr, gs[k], d.w_in[idx + k]);
+        d.w_out[idx + k] = w;
+        const uint16_t h = f32_to_bf16_rn(w);
         for (int r2 = 0; r2 < dp->world; ++r2)
           reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off)[idx + k] = h;
       }

@@ -112,6 +112,11 @@ template <int N>
 __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
+// Starts moving `bytes` (a multiple of 16; 16-byte aligned address) of global
+// memory into L2 without waiting for it.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* gptr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gptr), "r"(bytes) : "memory");
+}
 // Starts moving one box of a 2D tensor map into L2 without waiting for it
 // (x * element size must be a multiple of 16 bytes).
 __device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
