@@ -8,7 +8,10 @@ MSE, SGD lr=1e-3 (the configuration the headline metric is quoted on). N>1:
 data parallel, the same model with 8192 rows per GPU (weak scaling); by default
 (--dp fused) one launch per step on every rank, the weight-gradient tiles
 reduced inside it over peer memory (NVLink); --dp nccl: fp32 gradients
-all-reduced with NCCL between the backward and the update launch.
+all-reduced with NCCL between the backward and the update launch; --dp
+nccl-overlap: one NCCL all-reduce per layer on a side stream, each issued when
+its layer's gradient is complete and overlapped with the rest of the backward
+(the step in L launches, the grid leaving --reserve-sms SMs to NCCL).
 One JSON line on rank 0.
 """
 import argparse
@@ -224,7 +227,7 @@ def run_ours(args, cfg_name, cfg):
 
     dims, B = cfg["dims"], cfg["batch"]
     # fused data parallel needs bf16 weights; TF32 configs use the NCCL path
-    nccl_dp = ws > 1 and (args.dp == "nccl" or cfg["dtype"] != "bf16")
+    nccl_dp = ws > 1 and (args.dp in ("nccl", "nccl-overlap") or cfg["dtype"] != "bf16")
 
     def make_engine(gm):
         return pkt_b200.MLP(dims, B, dtype=cfg["dtype"], lr=cfg["lr"], bias=True, grad_mode=gm,
@@ -280,12 +283,34 @@ def run_ours(args, cfg_name, cfg):
     copy_stream = torch.cuda.Stream()
     sp = stream.cuda_stream
     grad_t = None
+    overlap = nccl_dp and args.dp == "nccl-overlap"
+    L = len(dims) - 1
     if nccl_dp:
         gptr, gcount = eng.grad_buffer()
         grad_t = _wrap_device_f32(gptr, gcount, local)
+    if overlap:
+        # one all-reduce per layer on a side stream, issued as soon as the
+        # segment that completes the layer's gradient has run, overlapped with the
+        # following segments; the persistent grid leaves SMs free for NCCL
+        eng.set_reserved_sms(args.reserve_sms)
+        side = torch.cuda.Stream()
+        seg_done = [torch.cuda.Event() for _ in range(L)]
+        buckets = []
+        for s_ in range(L):
+            o, n = eng.grad_bucket(L - 1 - s_)
+            buckets.append(grad_t[o:o + n])
 
     def step(s_ptr, n=1):
-        if nccl_dp:
+        if overlap:
+            for s_ in range(L):
+                eng.forward_backward_segment(s_, s_ptr)
+                seg_done[s_].record(stream)
+                side.wait_event(seg_done[s_])
+                with torch.cuda.stream(side):
+                    dist.all_reduce(buckets[s_])
+            stream.wait_stream(side)
+            eng.apply_update(s_ptr)
+        elif nccl_dp:
             eng.forward_backward(s_ptr)
             with torch.cuda.stream(stream):
                 dist.all_reduce(grad_t)
@@ -297,8 +322,8 @@ def run_ours(args, cfg_name, cfg):
     # (pkt_mlp_train with n >= 4 steps), the rest one launch per step.
     MULTI = 4
     group = MULTI if (ws == 1 and not nccl_dp and args.steps % MULTI == 0) else 1
-    launches = (args.steps // group) * (2 if nccl_dp else 1)
-    launches_per_step = 2 if nccl_dp else 1
+    launches_per_step = (L + 1) if overlap else (2 if nccl_dp else 1)
+    launches = (args.steps // group) * launches_per_step
     # ---------------- device-resident timing
     eng.load_batch_ptr(host_x[0].data_ptr(), host_t[0].data_ptr(), 0, sp)
     for _ in range(args.warmup):
@@ -427,7 +452,7 @@ def run_ours(args, cfg_name, cfg):
         "data": "synthetic (seeded N(0,1) inputs/targets, Kaiming-uniform weights, zero bias)",
         "config": {"workload": cfg_name + ": " + cfg["desc"], "global_batch": B * ws,
                    "per_gpu_batch": B,
-                   "parallelism": (f"dp{ws} ({'NCCL all-reduce' if nccl_dp else 'fused peer-memory reduce'})"
+                   "parallelism": (f"dp{ws} ({('NCCL all-reduce per layer, overlapped' if overlap else 'NCCL all-reduce') if nccl_dp else 'fused peer-memory reduce'})"
                                    if ws > 1 else "single GPU"),
                    "l2": "no flush: every step streams > 126 MB (weights, activations, gradients "
                          "exceed L2)", "launches_per_step": launches / args.steps,
@@ -475,9 +500,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--dp", default="fused", choices=["fused", "nccl"],
+    ap.add_argument("--reserve-sms", type=int, default=16,
+                    help="--dp nccl-overlap: SMs the step's grid leaves to NCCL")
+    ap.add_argument("--dp", default="fused", choices=["fused", "nccl", "nccl-overlap"],
                     help="N>1: weight gradients reduced inside the step launch over peer memory "
-                         "(fused) or by an NCCL all-reduce between two launches (nccl)")
+                         "(fused), by an NCCL all-reduce between two launches (nccl), or by one NCCL "
+                         "all-reduce per layer overlapped with the backward (nccl-overlap)")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: the configuration's batch on every GPU; strong: its global batch "
                          "(cfg4: 65536) split evenly over the GPUs")

@@ -334,6 +334,18 @@ int pkt_mlp_grad_buffer(pkt_mlp* m, float** ptr, long long* count);
 int pkt_mlp_set_grad_scale(pkt_mlp* m, float scale);
 int pkt_mlp_forward_backward(pkt_mlp* m, void* stream);
 int pkt_mlp_apply_update(pkt_mlp* m, void* stream);
+/* The same step as pkt_mlp_forward_backward in L launches (grad_mode 1), so the
+ * caller can all-reduce each layer's gradient on another stream as soon as it is
+ * complete, overlapped with the rest of the backward: after segment s (0..L-1)
+ * the bucket of layer L-1-s (pkt_mlp_grad_bucket: offset and count in floats
+ * within pkt_mlp_grad_buffer, dW then db) is final. Segment 0 also runs the
+ * forward and the loss. pkt_mlp_set_reserved_sms leaves that many SMs out of
+ * the persistent grid, so a collective kernel on another stream has SMs to run
+ * on while a segment runs (0 by default). */
+int pkt_mlp_backward_segments(pkt_mlp* m, int* count);
+int pkt_mlp_forward_backward_segment(pkt_mlp* m, int segment, void* stream);
+int pkt_mlp_grad_bucket(pkt_mlp* m, int layer, long long* offset, long long* count);
+int pkt_mlp_set_reserved_sms(pkt_mlp* m, int sms);
 /* Fused data parallel (grad_mode 2): one launch per step on every rank; the
  * weight-gradient tiles go to their owner rank (tile index mod world) over
  * peer memory as they finish, the owner sums the ranks' partials in rank

@@ -110,6 +110,10 @@ _SIGS = {
     "pkt_mlp_dp_connect": ([_P, c_int, c_int, _P], c_int),
     "pkt_mlp_forward_backward": ([_P, _P], c_int),
     "pkt_mlp_apply_update": ([_P, _P], c_int),
+    "pkt_mlp_backward_segments": ([_P, ctypes.POINTER(c_int)], c_int),
+    "pkt_mlp_forward_backward_segment": ([_P, c_int, _P], c_int),
+    "pkt_mlp_grad_bucket": ([_P, c_int, ctypes.POINTER(c_longlong), ctypes.POINTER(c_longlong)], c_int),
+    "pkt_mlp_set_reserved_sms": ([_P, c_int], c_int),
     "pkt_mlp_set_perf": ([_P, c_int], c_int),
     "pkt_mlp_fetch_perf": ([_P, _P, c_int, ctypes.POINTER(c_int)], c_int),
     "pkt_mlp_clock_stats": ([_P, _P, c_int], c_int),

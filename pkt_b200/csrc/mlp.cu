@@ -95,7 +95,7 @@ struct Mlp {
   int loss_cap = 1 << 16;
   int losses_enqueued = 0;
   float* Yout = nullptr;
-  float* grads = nullptr;  // grad_mode 1: flat [dW_0 .. dW_{L-1}, db_0 .. db_{L-1}]
+  float* grads = nullptr;  // grad_mode 1: per layer one bucket [dW_l, db_l], layer 0 first
   long long grad_count = 0;
   std::vector<long long> dW_off, db_off;
 
@@ -112,6 +112,13 @@ struct Mlp {
   pkt_task* d_multi[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
   int wg_token_base = 0;  // token of layer 0's weight-gradient tiles (layer l: + l)
   pkt_task* d_update[2] = {nullptr, nullptr};
+  // grad_mode 1: the step list split into L backward segments (segment s ends
+  // with layer L-1-s's gradient complete), by weight parity and input slot;
+  // seg_begin[p][q][s] is the first task of segment s (L + 1 entries)
+  std::vector<pkt_task> segs[2][2];
+  std::vector<int> seg_begin[2][2];
+  pkt_task* d_segs[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
+  int reserved_sms = 0;  // SMs the persistent grid leaves free (for a collective on another stream)
   int num_tokens = 0;
   int gemm_tiles_per_step = 0;
   double flops_per_step = 0;
@@ -140,6 +147,8 @@ struct Mlp {
       F(d_tasks[k][1]);
       F(d_multi[k][0]);
       F(d_multi[k][1]);
+      F(d_segs[k][0]);
+      F(d_segs[k][1]);
     }
     for (auto p : H) F(p);
     for (auto p : dY) F(p);
@@ -289,11 +298,9 @@ int Mlp::setup(const pkt_mlp_config& c) {
     dW_off.resize(L);
     db_off.resize(L);
     long long o = 0;
-    for (int l = 0; l < L; ++l) {
+    for (int l = 0; l < L; ++l) {  // contiguous per layer: one all-reduce bucket each
       dW_off[l] = o;
       o += (long long)dims[l + 1] * ld[l];
-    }
-    for (int l = 0; l < L; ++l) {
       db_off[l] = o;
       o += round_up(dims[l + 1], 4);
     }
@@ -845,7 +852,100 @@ int Mlp::build(int p, int q) {
       }
     }
   }
+  // ---- backward segments (grad_mode 1): the same tasks as the step list, in
+  // its order, split into L launches so that a caller can all-reduce layer l's
+  // gradient bucket on another stream while the following segments run (one
+  // collective per layer, overlapped with the rest of the backward). Segment 0
+  // holds the forward, the loss and layer L-1's weight / bias gradient; segment
+  // s >= 1 the dgrad tiles that produce dY_l and layer l's gradient, l = L-1-s.
+  // A launch starts with its tokens at zero, so every dependency count drops by
+  // the publishes earlier segments made (complete: stream order) and a count
+  // they already satisfied disappears.
+  std::vector<pkt_task>& sl = segs[p][q];
+  std::vector<int>& sb = seg_begin[p][q];
+  sl.clear();
+  sb.clear();
+  if (grad_mode == 1) {
+    auto seg_of = [&](const pkt_task& t) -> int {
+      const uint16_t op = t.header.opcode;
+      if (op == PKT_OP_GEMM) {
+        pkt_gemm_tile_args a;
+        std::memcpy(&a, t.args, sizeof(a));
+        const int gi = int(a.gemm) - first;
+        for (int l = 0; l < L; ++l) {
+          if (gi == fwd[l]) return 0;
+          if (gi == wgr[l]) return L - 1 - l;
+          if (l >= 1 && gi == dgr[l]) return L - l;  // it produces dY_{l-1}
+        }
+        return -1;
+      }
+      if (op == PKT_OP_BIAS_SGD) {
+        pkt_bias_sgd_args a;
+        std::memcpy(&a, t.args, sizeof(a));
+        for (int l = 0; l < L; ++l)
+          if (a.partials == colsum[l]) return L - 1 - l;
+        return -1;
+      }
+      if (op == PKT_OP_LOSS_REDUCE) return 0;
+      return -1;
+    };
+    std::vector<int> seg(tl.size());
+    std::vector<std::vector<int>> pub(L, std::vector<int>(num_tokens, 0));
+    for (size_t i = 0; i < tl.size(); ++i) {
+      seg[i] = seg_of(tl[i]);
+      if (seg[i] < 0) return fail(PKT_ERR_UNSUPPORTED, "task %zu has no backward segment", i);
+      const pkt_task_header& h = tl[i].header;
+      if (h.read_epoch != 0) return fail(PKT_ERR_UNSUPPORTED, "segmented lists take no epochs");
+      if (h.buffer_write_id) pub[seg[i]][h.buffer_write_id]++;
+      if (h.ext_ids >> 16) pub[seg[i]][h.ext_ids >> 16]++;
+    }
+    // returns false when a count needs publishes of a later segment
+    auto adjust = [&](int s, int tok, uint32_t need, int* id_out, uint32_t* need_out) {
+      int before = 0;
+      for (int k = 0; k < s; ++k) before += pub[k][tok];
+      if (int(need) <= before) {
+        *id_out = 0;
+        *need_out = 0;
+        return true;
+      }
+      *id_out = tok;
+      *need_out = need - uint32_t(before);
+      return int(*need_out) <= pub[s][tok];
+    };
+    for (int s = 0; s < L; ++s) {
+      sb.push_back(int(sl.size()));
+      for (size_t i = 0; i < tl.size(); ++i) {
+        if (seg[i] != s) continue;
+        pkt_task t = tl[i];
+        pkt_task_header& h = t.header;
+        int id = 0;
+        uint32_t need = 0;
+        if (h.buffer_read_id) {
+          if (!adjust(s, h.buffer_read_id, h.wait_count, &id, &need))
+            return fail(PKT_ERR_UNSUPPORTED, "task %zu waits for a later segment", i);
+          h.buffer_read_id = uint16_t(id);
+          h.wait_count = need;
+        }
+        if (h.ext_ids & 0xffffu) {
+          if (!adjust(s, int(h.ext_ids & 0xffffu), h.ext_wait_count, &id, &need))
+            return fail(PKT_ERR_UNSUPPORTED, "task %zu waits for a later segment", i);
+          h.ext_ids = (h.ext_ids & 0xffff0000u) | uint32_t(id);
+          h.ext_wait_count = need;
+        }
+        sl.push_back(t);
+      }
+    }
+    sb.push_back(int(sl.size()));
+  }
   // ---- device copies
+  cudaFree(d_segs[p][q]);
+  d_segs[p][q] = nullptr;
+  if (!sl.empty()) {
+    cudaError_t e = cudaMalloc(&d_segs[p][q], sizeof(pkt_task) * sl.size());
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(segment tasks)");
+    e = cudaMemcpy(d_segs[p][q], sl.data(), sizeof(pkt_task) * sl.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "copy segment tasks");
+  }
   cudaFree(d_tasks[p][q]);
   cudaFree(d_update[p]);
   d_tasks[p][q] = d_update[p] = nullptr;
@@ -952,7 +1052,7 @@ int Mlp::launch_list(pkt_task* d, int n, cudaStream_t st) {
   }
   kp.clock_acc = rt->d_clock;
   int blocks = 0;
-  int rc = rt->clamp_blocks(rt->num_sms, P, &blocks);
+  int rc = rt->clamp_blocks(std::max(P, rt->num_sms - reserved_sms), P, &blocks);
   if (rc) return rc;
   rc = rt->trace_for(n, st, &kp.trace);
   if (rc) return rc;
@@ -1174,6 +1274,47 @@ int pkt_mlp_apply_update(pkt_mlp* h, void* stream) {
   int rc = m->launch_list(m->d_update[p], int(m->update[p].size()), static_cast<cudaStream_t>(stream));
   if (rc) return rc;
   m->parity ^= 1;
+  return PKT_OK;
+}
+
+int pkt_mlp_backward_segments(pkt_mlp* h, int* count) {
+  if (!h || !count) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  if (h->m->grad_mode != 1) return pkb::fail(PKT_ERR_ARGS, "backward segments exist with grad_mode 1 only");
+  *count = h->m->L;
+  return PKT_OK;
+}
+
+int pkt_mlp_forward_backward_segment(pkt_mlp* h, int segment, void* stream) {
+  if (!h) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  if (m->grad_mode != 1) return pkb::fail(PKT_ERR_ARGS, "backward segments exist with grad_mode 1 only");
+  if (segment < 0 || segment >= m->L) return pkb::fail(PKT_ERR_ARGS, "segment %d of %d", segment, m->L);
+  const int p = m->parity, q = m->active_slot;
+  const std::vector<int>& sb = m->seg_begin[p][q];
+  if (int(sb.size()) != m->L + 1) return pkb::fail(PKT_ERR_ARGS, "segments not built");
+  if (segment == 0) {
+    if (m->losses_enqueued + 1 > m->loss_cap) return pkb::fail(PKT_ERR_ARGS, "loss buffer full");
+    m->losses_enqueued++;
+  }
+  cudaSetDevice(m->rt->device);
+  return m->launch_list(m->d_segs[p][q] + sb[segment], sb[segment + 1] - sb[segment],
+                        static_cast<cudaStream_t>(stream));
+}
+
+int pkt_mlp_grad_bucket(pkt_mlp* h, int layer, long long* offset, long long* count) {
+  if (!h || !offset || !count) return pkb::fail(PKT_ERR_ARGS, "null argument");
+  Mlp* m = h->m;
+  if (m->grad_mode != 1) return pkb::fail(PKT_ERR_ARGS, "gradient buffer exists with grad_mode 1 only");
+  if (layer < 0 || layer >= m->L) return pkb::fail(PKT_ERR_ARGS, "layer %d of %d", layer, m->L);
+  *offset = m->dW_off[layer];
+  *count = (layer + 1 < m->L ? m->dW_off[layer + 1] : m->grad_count) - m->dW_off[layer];
+  return PKT_OK;
+}
+
+int pkt_mlp_set_reserved_sms(pkt_mlp* h, int sms) {
+  if (!h || sms < 0) return pkb::fail(PKT_ERR_ARGS, "bad argument");
+  if (sms > h->m->rt->num_sms - 2) return pkb::fail(PKT_ERR_ARGS, "the grid needs at least 2 SMs");
+  h->m->reserved_sms = sms;
   return PKT_OK;
 }
 

@@ -137,6 +137,27 @@ class MLP:
     def apply_update(self, stream=None):
         check(self._L.pkt_mlp_apply_update(self._h, stream))
 
+    def backward_segments(self):
+        """Number of launches the segmented step takes (grad_mode 1): L."""
+        n = ctypes.c_int()
+        check(self._L.pkt_mlp_backward_segments(self._h, ctypes.byref(n)))
+        return n.value
+
+    def forward_backward_segment(self, segment, stream=None):
+        """Segment s of the step (grad_mode 1); after it, layer L-1-s's gradient
+        bucket (grad_bucket) is final and can be all-reduced on another stream."""
+        check(self._L.pkt_mlp_forward_backward_segment(self._h, int(segment), stream))
+
+    def grad_bucket(self, layer):
+        """(offset, count) in floats of layer `layer`'s dW and db in grad_buffer()."""
+        o, n = ctypes.c_longlong(), ctypes.c_longlong()
+        check(self._L.pkt_mlp_grad_bucket(self._h, int(layer), ctypes.byref(o), ctypes.byref(n)))
+        return o.value, n.value
+
+    def set_reserved_sms(self, sms):
+        """Leave `sms` SMs out of the persistent grid (room for a collective kernel)."""
+        check(self._L.pkt_mlp_set_reserved_sms(self._h, int(sms)))
+
     def grad_buffer(self):
         p, n = c_void_p(), ctypes.c_longlong()
         check(self._L.pkt_mlp_grad_buffer(self._h, ctypes.byref(p), ctypes.byref(n)))

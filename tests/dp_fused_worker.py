@@ -3,8 +3,10 @@
 Each rank trains the same small MLP on its own shard twice: through grad_mode 1
 (fp32 gradients, NCCL all-reduce, separate update launch) and through grad_mode
 2 (partial weight tiles sent to their owner rank over peer memory, reduced and
-applied inside the step launch). With two ranks a sum of two partials does not
-depend on order, so both paths must give the same bits. Results go to
+applied inside the step launch), and a third time through grad_mode 1 in
+backward segments, one NCCL all-reduce per layer on a side stream overlapped
+with the following segments. With two ranks a sum of two partials does not
+depend on order, so all paths must give the same bits. Results go to
 <out>/rank<r>.npz.
 """
 import os
@@ -66,6 +68,34 @@ def main():
     res["W1"], res["b1"] = [np.concatenate([a.ravel() for a in v]) for v in e1.get_params()]
     res["loss1"] = e1.losses()
     e1.close()
+
+    # ---- grad_mode 1 in backward segments: one all-reduce per layer, overlapped
+    e3 = pkt_b200.MLP(DIMS, BATCH, lr=LR, grad_mode=1, device=rank)
+    e3.set_grad_scale(1.0 / world)
+    e3.set_params(Ws, bs)
+    e3.load_batch(e3.storage_array(x), e3.storage_array(t))
+    e3.set_reserved_sms(16)
+    gptr, gcount = e3.grad_buffer()
+    g3 = wrap_f32(gptr, gcount, rank)
+    L = e3.backward_segments()
+    main_s = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    for _ in range(STEPS):
+        for s in range(L):
+            e3.forward_backward_segment(s)
+            ev = torch.cuda.Event()
+            ev.record(main_s)
+            side.wait_event(ev)
+            o, n = e3.grad_bucket(L - 1 - s)
+            with torch.cuda.stream(side):
+                dist.all_reduce(g3[o:o + n])
+        main_s.wait_stream(side)
+        e3.apply_update()
+    torch.cuda.synchronize()
+    res["status3"] = np.array(e3.status())
+    res["W3"], res["b3"] = [np.concatenate([a.ravel() for a in v]) for v in e3.get_params()]
+    res["loss3"] = e3.losses()
+    e3.close()
 
     # ---- grad_mode 2: fused over peer memory
     e2 = pkt_b200.MLP(DIMS, BATCH, lr=LR, grad_mode=2, device=rank)
