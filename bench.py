@@ -56,9 +56,9 @@ def flops_per_sample(dims):
 # from one ncu capture of that config; the capture is summarised, with its
 # command, in the named profile.
 PROFILED_TRAFFIC = {
-    "cfg2": {"bytes": 2.104e9 + 0.664e9,
-             "source": "dram__bytes_read.sum + dram__bytes_write.sum of one pk_megakernel launch "
-                       "(one cfg2 step) in a separate ncu capture of this configuration; a fixed "
+    "cfg2": {"bytes": (13.157e9 + 2.676e9) / 4,
+             "source": "dram__bytes_read.sum + dram__bytes_write.sum of one 4-step pk_megakernel "
+                       "launch in a separate ncu capture of this configuration, per step; a fixed "
                        "figure, not measured in this run"},
 }
 

@@ -170,6 +170,12 @@ __device__ __forceinline__ void publish_slot(SmemT<P>& s, int slot, const pkt_ta
 }
 
 // ============================================================ controller
+// Pause between two polls of a dependency token (ns; 0 = spin).
+#ifndef PKT_POLL_SLEEP_NS
+#define PKT_POLL_SLEEP_NS 32
+#endif
+constexpr unsigned kPollSleepNs = PKT_POLL_SLEEP_NS;
+
 template <int P, class Ops>
 __device__ void controller_loop(const KParams& p, SmemT<P>& s, unsigned long long* perf) {
   int seq = 0;
@@ -241,7 +247,7 @@ __device__ void controller_loop(const KParams& p, SmemT<P>& s, unsigned long lon
             break;
           }
         }
-        __nanosleep(32);
+        if (kPollSleepNs > 0) __nanosleep(kPollSleepNs);
       }
       dep_cycles += clock64() - c0;
       if (!ok) break;
@@ -1523,13 +1529,14 @@ __device__ void compute_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base, 
     }
     if (tr) tr[kTrDone] = globaltimer_ns();
     // ---- publish completion. Every thread's stores are ordered before the
-    // barrier; thread 0 then makes them visible at gpu scope with one fence
-    // (cumulative over what the barrier ordered before it) and releases the
-    // token. The proxy fence orders this thread's async-proxy (TMA store) writes,
-    // complete by now, with the generic release.
+    // barrier; thread 0's release of the token is cumulative over what the
+    // barrier ordered before it, so it needs no separate fence. The proxy fence
+    // orders this thread's async-proxy (TMA store) writes, complete by now, with
+    // the generic release. In a pair the other CTA fences its half at gpu scope
+    // before it signals the leader.
     fence_proxy_async_global();
     epi_sync();
-    if (c.et == 0) __threadfence();
+    if (P == 2 && c.et == 0 && c.rank != 0) __threadfence();
     if (P == 2 && c.et == 0) {
       // pair: the leader publishes once the other CTA's half is stored too
       const int ps = (seq - 1) % kSlots;

@@ -63,8 +63,9 @@ def axpy_report(args):
 def sgd_report(args):
     """SGDMixed tasks (fp32 master w -= lr * g in place, bf16 copy of the new w
     written alongside: 14 bytes per parameter -- read w, read g, write w, write
-    the copy) over N parameters already on the device, in chunks of 2^20 per task,
-    one persistent launch per pass (the grad_mode 1 update pass of the MLP engine)."""
+    the copy) over N parameters already on the device, in chunks of 2^16 per task
+    (as the MLP engine's grad_mode 1 update list; many tasks per SM, so the last
+    wave is short), one persistent launch per pass."""
     import torch
     import pkt_b200
     from pkt_b200 import runtime as R
@@ -74,7 +75,7 @@ def sgd_report(args):
     w = torch.rand(n, device="cuda")
     g = torch.rand(n, device="cuda") * 1e-3
     wb = torch.empty(n, dtype=torch.bfloat16, device="cuda")
-    chunk = 1 << 20
+    chunk = 1 << 16
     ntask = (n + chunk - 1) // chunk
     tasks = R.make_tasks(ntask)
     for i in range(ntask):
