@@ -698,12 +698,6 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
                               int tile_m, int tile_n, uint32_t tmem_base, uint32_t acc,
                               uint32_t use, unsigned long long& tmem_wait, uint32_t tix) {
   const pkt_gemm_desc& d = g.d;
-  const long long c0 = clock64();
-  wait_bar(p, &s.tmem_full[acc], use & 1, 8);
-  tmem_wait += clock64() - c0;
-  if (p.trace && c.et == 0 && c.rank == 0) p.trace[(size_t)tix * kTraceWords + kTrExec] = globaltimer_ns();
-  __syncwarp();  // tcgen05.ld is warp-collective
-  tc_fence_after();
 
   // Every descriptor field the chunk loop uses goes to registers first: the
   // "memory" clobber of each tcgen05.ld would otherwise make the compiler
@@ -821,7 +815,23 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
       for (int j = 0; j < 32; ++j) a[j] = 0.f;
     }
   };
+  // bias of a chunk's 32 columns: one coalesced load per warp, broadcast by
+  // shuffles; chunk ch+1's is loaded while chunk ch is processed
+  auto bias_issue = [&](int ch2) -> float {
+    const int col = n0 + ch2 * 32 + c.lane;
+    return (add_bias && col < N) ? __ldg(bias + col) : 0.f;
+  };
+  // The first chunk's loads (aux rows, bias) go out before the accumulator
+  // wait, so their latency overlaps the end of the mainloop.
   bool auxq_ready = aux_issue(0);
+  float bl_next = bias_issue(0);
+
+  const long long c0 = clock64();
+  wait_bar(p, &s.tmem_full[acc], use & 1, 8);
+  tmem_wait += clock64() - c0;
+  if (p.trace && c.et == 0 && c.rank == 0) p.trace[(size_t)tix * kTraceWords + kTrExec] = globaltimer_ns();
+  __syncwarp();  // tcgen05.ld is warp-collective
+  tc_fence_after();
 
   // TMEM reads are double-buffered: chunk ch+1 is in flight while chunk ch is
   // processed and stored.
@@ -840,9 +850,8 @@ __device__ void epilogue_gemm(const KParams& p, SmemT<P>& s, const EpiCtx& c, co
     nvalid = nvalid < 0 ? 0 : (nvalid > 32 ? 32 : nvalid);
     if (!row_ok) nvalid = 0;
 
-    // bias of the chunk's 32 columns: one coalesced load, broadcast by shuffles
-    float bl = 0.f;
-    if (add_bias && col0 + c.lane < N) bl = __ldg(bias + col0 + c.lane);
+    const float bl = bl_next;
+    if (more) bl_next = bias_issue(ch + 1);
 
     if (epi == PKT_EPI_STORE || epi == PKT_EPI_WGRAD_STORE) {
       emit_out(v, col0, nvalid);
