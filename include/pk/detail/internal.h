@@ -163,6 +163,9 @@ struct KParams {
   unsigned long long timeout_ns;
   const DpPeers* dp;  // fused data parallel (null otherwise)
   int dp_step;        // fused data-parallel steps completed before this launch
+  // >0: a controller dequeues its next task only while fewer than this many of
+  // the tasks it published wait for its compute warps (0: the slot ring alone)
+  int lookahead;
   // optional [3]: += SM cycles, += nanoseconds of CTA 0's lifetime, += 1 per launch
   unsigned long long* clock_acc;
   // optional [num_tasks][kTraceWords]: per task, %globaltimer stamps of its stages

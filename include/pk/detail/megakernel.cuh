@@ -68,6 +68,7 @@ struct SmemT {
   uint64_t pair_done[kSlots];  // leader: the other CTA of the pair finished task seq
   uint32_t tmem_base;
   int dp_ok;  // PKT_OP_DP_REDUCE: every rank's partial of the current tile arrived
+  int taken;  // tasks the compute warps have taken from the slot ring (leader CTA)
   pk::PipelineSlot user_slot;                  // the task a pk::OpTraits op sees as br.slot(0)
   pk::PageMeta page_meta[pk::Config::kPagesPerSlot];  // leases / tags of its pages (in epi_stage)
   float red[8][4][32];  // per 32-column chunk, per TMEM lane quadrant: column partial sums
@@ -183,6 +184,27 @@ __device__ void controller_loop(const KParams& p, SmemT<P>& s, unsigned long lon
   int cursor_local = 0, cursor_end = 0;
   while (true) {
     if (*status_word(p) != 0) break;
+    if (p.lookahead > 0) {
+      // A task this CTA holds is a task no idle CTA can take: dequeue the next one
+      // only when the pipeline is about to need it.
+      const long long c1 = clock64();
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t it = 0;
+      bool ok = true;
+      while (seq - *reinterpret_cast<volatile int*>(&s.taken) >= p.lookahead) {
+        if ((++it & 63u) == 0) {
+          if (*status_word(p) != 0 || globaltimer_ns() - t0 > p.timeout_ns) {
+            ok = false;
+            break;
+          }
+        }
+      }
+      slot_cycles += clock64() - c1;
+      if (!ok) {
+        if (*status_word(p) == 0) set_error(p, PKT_DEV_TIMEOUT_DEPS, -1, -4);
+        break;
+      }
+    }
     if (cursor_local >= cursor_end) {
       const int start = atomicAdd(p.state, p.chunk);
       cursor_local = start;
@@ -1464,6 +1486,7 @@ __device__ void compute_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base, 
     epi_sync();  // every compute thread has its copy
     if (c.et == 0) release_slot<P>(s, slot, c.rank);
     ++seq;
+    if (c.et == 0 && c.rank == 0) *reinterpret_cast<volatile int*>(&s.taken) = seq;
     const uint16_t op = task.header.opcode;
     if (op == kOpStop) break;
     const long long c0 = clock64();
@@ -1601,6 +1624,7 @@ __global__ void __launch_bounds__(kThreads, 1) pk_megakernel(const __grid_consta
       mbar_init(&s.pair_done[i], 1);
     }
     for (int i = 0; i < pk::Config::kPagesPerSlot; ++i) s.page_meta[i].reset();
+    s.taken = 0;
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.tmem_full[i], 1);
       mbar_init(&s.tmem_empty[i], 4 * P);  // one arrive per compute warp (of both CTAs)
