@@ -1255,13 +1255,76 @@ __device__ void op_linear_backward(const LinearBackwardArgs& a, int et, int nthr
   }
 }
 
+// Column sums of `num` partial rows (row stride ld floats), summed from row 0
+// up -- the order every path of the engine uses, so their results are
+// bit-identical. Eight rows' loads are in flight before any is added.
+__device__ __forceinline__ float column_sum_in_order(const float* partials, int num, long long ld, int col) {
+  float sum = 0.f;
+  int r = 0;
+  for (; r + 8 <= num; r += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __ldcg(partials + (long long)(r + j) * ld + col);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sum += v[j];
+  }
+  for (; r < num; ++r) sum += __ldcg(partials + (long long)r * ld + col);
+  return sum;
+}
+
+// The same for four adjacent columns (col and ld multiples of 4, partials 16-byte aligned).
+__device__ __forceinline__ float4 column_sum4_in_order(const float* partials, int num, long long ld, int col) {
+  float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+  int r = 0;
+  for (; r + 8 <= num; r += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __ldcg(reinterpret_cast<const float4*>(partials + (long long)(r + j) * ld + col));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sum.x += v[j].x;
+      sum.y += v[j].y;
+      sum.z += v[j].z;
+      sum.w += v[j].w;
+    }
+  }
+  for (; r < num; ++r) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(partials + (long long)r * ld + col));
+    sum.x += v.x;
+    sum.y += v.y;
+    sum.z += v.z;
+    sum.w += v.w;
+  }
+  return sum;
+}
+
+// Calls f(col, sum) for every column of [c0, c1), the columns spread over the
+// task's threads four at a time where the layout allows.
+template <class F>
+__device__ __forceinline__ void for_column_sums(const float* partials, int num, long long ld, int c0, int c1,
+                                                int et, int nthr, F&& f) {
+  if (aligned16(partials) && (ld & 3) == 0 && (c0 & 3) == 0) {
+    for (int col = c0 + 4 * et; col < c1; col += 4 * nthr) {
+      if (col + 4 <= c1) {
+        const float4 v = column_sum4_in_order(partials, num, ld, col);
+        f(col, v.x);
+        f(col + 1, v.y);
+        f(col + 2, v.z);
+        f(col + 3, v.w);
+      } else {
+        for (int k = col; k < c1; ++k) f(k, column_sum_in_order(partials, num, ld, k));
+      }
+    }
+  } else {
+    for (int col = c0 + et; col < c1; col += nthr) f(col, column_sum_in_order(partials, num, ld, col));
+  }
+}
+
 __device__ void op_bias_sgd(const pkt_bias_sgd_args& a, int et, int nthr) {
-  for (int col = a.col_begin + et; col < a.col_end; col += nthr) {
-    float sum = 0.f;
-    for (int pidx = 0; pidx < a.num_partials; ++pidx) sum += a.partials[(long long)pidx * a.ld + col];
+  for_column_sums(a.partials, a.num_partials, a.ld, a.col_begin, a.col_end, et, nthr, [&](int col, float sum) {
     if (a.grad_out) a.grad_out[col] = sum;
     if (a.bias) a.bias[col] = fmaf(-a.lr, sum, a.bias[col]);
-  }
+  });
 }
 
 // ============================================================ fused data parallel
@@ -1319,7 +1382,23 @@ __device__ void op_dp_reduce(const KParams& p, SmemT<P>& s, const EpiCtx& c, con
     // (world + 1) 16-byte loads in flight per thread instead of one dependent
     // chain, which is what bounds this pass (it moves ~20 bytes per element).
     constexpr int U = 8;
-    for (int e0 = c.tid; e0 < total; e0 += U * c.nthr) {
+    // Full 256-column rows: every 64 consecutive threads hold one row, so a
+    // pass leaves U x 2 whole rows in this CTA. Their bf16 values are staged in
+    // shared memory (two 8 KB pass buffers in the epilogue staging area) and
+    // sent to the other ranks as one 512-byte bulk copy per row and rank;
+    // 8-byte stores from the threads into peer memory ran at ~1 GB/s per SM.
+    const bool bulk = cols == 256 && dp->world > 1 && (c.nthr & 127) == 0 && (shadow_off & 15) == 0 &&
+                      ((ldw * 2) & 15) == 0;
+    uint8_t* const stage = &s.epi_stage[0][0];
+    static_assert(4 * kEpiStageBytes >= 2 * U * 2 * 512, "pass buffers exceed the staging area");
+    const int npass = (total + U * c.nthr - 1) / (U * c.nthr);
+    for (int pass = 0; pass < npass; ++pass) {
+      const int e0 = c.tid + pass * U * c.nthr;
+      uint8_t* const buf = stage + (pass & 1) * (U * 2 * 512);
+      if (bulk && pass >= 2) {
+        if (c.et == 0) bulk_wait_read<1>();  // pass-2's copies have read this buffer
+        epi_sync();
+      }
       float4 gs[U], wv[U];
       int soff[U];
       long long idx[U];
@@ -1354,9 +1433,35 @@ __device__ void op_dp_reduce(const KParams& p, SmemT<P>& s, const EpiCtx& c, con
         w.w = fmaf(-lr, gs[u].w, wv[u].w);
         *reinterpret_cast<float4*>(d.w_out + idx[u]) = w;
         const uint2 pk = make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
-        for (int r2 = 0; r2 < dp->world; ++r2)
-          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + idx[u]) = pk;
+        if (bulk) {
+          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(own + shadow_off) + idx[u]) = pk;
+          *reinterpret_cast<uint2*>(buf + (u * 2 + (c.et >> 6)) * 512 + (c.et & 63) * 8) = pk;
+        } else {
+          for (int r2 = 0; r2 < dp->world; ++r2)
+            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + idx[u]) = pk;
+        }
       }
+      if (bulk) {
+        fence_proxy_async_smem();
+        epi_sync();
+        if (c.et == 0) {
+          for (int u = 0; u < U; ++u)
+            for (int h = 0; h < 2; ++h) {
+              const int er = pass * U * c.nthr + u * c.nthr + int(c.rank) * kEpiThreads + h * 64;
+              if (er >= total) continue;
+              const long long ridx = (long long)(row0 + er / cg) * ldw + n0;
+              for (int r2 = 0; r2 < dp->world; ++r2)
+                if (r2 != dp->rank)
+                  bulk_store_1d(reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + ridx,
+                                buf + (u * 2 + h) * 512, 512);
+            }
+          bulk_commit();
+        }
+      }
+    }
+    if (bulk && c.et == 0) {
+      bulk_wait_all();  // the copies have landed in the peers' memory
+      fence_proxy_async_global();
     }
   } else {
     for (int e = c.tid; e < total; e += c.nthr) {
@@ -1391,12 +1496,10 @@ __device__ void op_dp_bias_send(const KParams& p, const EpiCtx& c, const pkt_dp_
   if (dp == nullptr) return;
   const int par = p.dp_step & 1;
   const long long off = ((long long)(par * dp->world + dp->rank)) * dp->bias_total + a.bias_off;
-  for (int col = c.tid; col < a.n; col += c.nthr) {
-    float sum = 0.f;
-    for (int pidx = 0; pidx < a.num_partials; ++pidx) sum += a.partials[(long long)pidx * a.ld + col];
+  for_column_sums(a.partials, a.num_partials, a.ld, 0, a.n, c.tid, c.nthr, [&](int col, float sum) {
     for (int r2 = 0; r2 < dp->world; ++r2)
       reinterpret_cast<float*>(dp->base[r2] + dp->bias_recv_off)[off + col] = sum;
-  }
+  });
   __threadfence_system();
   epi_sync();
   if (c.et == 0)

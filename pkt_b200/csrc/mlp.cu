@@ -708,10 +708,12 @@ int Mlp::build(int p, int q) {
     // tiles, so partial tiles cross to their owners (and the owners' new
     // weights back) while the rest of the backward runs. A weight-gradient
     // epilogue only sends its partial; the owner's reduce task of a tile (sum,
-    // SGD, new bf16 tile to every rank) is listed in the next layer's dgrad block,
-    // after two waves of it (layer 0's last): by then every rank has normally
-    // sent its partial, so the reduce rarely waits, and no GEMM epilogue ever
-    // waits on another rank.
+    // SGD, new bf16 tile to every rank) is listed after the next layer's whole
+    // dgrad block (layer 1's after layer 0's weight-gradient tiles, layer 0's
+    // last): a weight-gradient tile of the wide layers runs ~75 us, and a reduce
+    // dequeued before the ranks' partials have landed holds its CTA pair
+    // waiting (listed two dgrad waves later, the reduces averaged 57 us each on
+    // two GPUs, mostly waiting). No GEMM epilogue ever waits on another rank.
     const float lre = lr * grad_scale;
     std::vector<pkt_task> deferred;  // this rank's reduce tasks of the previous layer
     std::vector<pkt_task> last;      // layer 0's reduce tasks
@@ -727,15 +729,7 @@ int Mlp::build(int p, int q) {
             t.header.ext_ids = uint32_t(BF[l - 1]) << 16;
             tl.push_back(t);
             ++tiles;
-            if (!deferred.empty() && (i * dg.tiles_n + j + 1) == 2 * std::max(1, rt->num_sms / P)) {
-              for (auto& d2 : deferred) tl.push_back(d2);
-              deferred.clear();
-            }
           }
-        for (auto& d2 : deferred) tl.push_back(d2);
-        deferred.clear();
-      } else {
-        // layer 0 has no dgrad block: layer 1's reduce tasks go right here
         for (auto& d2 : deferred) tl.push_back(d2);
         deferred.clear();
       }
@@ -760,6 +754,10 @@ int Mlp::build(int p, int q) {
               (l >= 1 ? deferred : last).push_back(r);
             }
           }
+      }
+      if (l == 0) {  // no dgrad block follows: layer 1's reduce tasks go here
+        for (auto& d2 : deferred) tl.push_back(d2);
+        deferred.clear();
       }
       if (has_bias) {
         pkt_task t{};
