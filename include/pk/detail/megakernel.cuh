@@ -1348,7 +1348,8 @@ __device__ void op_dp_wait(const KParams& p, const EpiCtx& c, const pkt_dp_wait_
 // (the status word is set) leaves the master and every copy as they were and
 // counts nothing, so the step fails without corrupting the weights.
 template <int P>
-__device__ void op_dp_reduce(const KParams& p, SmemT<P>& s, const EpiCtx& c, const pkt_gemm_tile_args& a) {
+__device__ void op_dp_reduce(const KParams& p, SmemT<P>& s, const EpiCtx& c, const pkt_gemm_tile_args& a,
+                             unsigned long long* tr) {
   const DpPeers* dp = p.dp;
   if (dp == nullptr || int(a.gemm) >= p.num_gemms) return;
   const DevGemm& g = p.gemms[a.gemm];
@@ -1362,6 +1363,7 @@ __device__ void op_dp_reduce(const KParams& p, SmemT<P>& s, const EpiCtx& c, con
   epi_sync();
   const bool ok = s.dp_ok != 0;
   epi_sync();  // every thread has read the flag before the next task may rewrite it
+  if (tr) tr[kTrLoad] = globaltimer_ns();  // (SIMT tasks have no loads: the wait's end)
   if (!ok) return;
   const int rows_tile = dp->pair * kBM;
   const int row0 = int(a.tile_m) * rows_tile, n0 = int(a.tile_n) * d.bn;
@@ -1382,23 +1384,7 @@ __device__ void op_dp_reduce(const KParams& p, SmemT<P>& s, const EpiCtx& c, con
     // (world + 1) 16-byte loads in flight per thread instead of one dependent
     // chain, which is what bounds this pass (it moves ~20 bytes per element).
     constexpr int U = 8;
-    // Full 256-column rows: every 64 consecutive threads hold one row, so a
-    // pass leaves U x 2 whole rows in this CTA. Their bf16 values are staged in
-    // shared memory (two 8 KB pass buffers in the epilogue staging area) and
-    // sent to the other ranks as one 512-byte bulk copy per row and rank;
-    // 8-byte stores from the threads into peer memory ran at ~1 GB/s per SM.
-    const bool bulk = cols == 256 && dp->world > 1 && (c.nthr & 127) == 0 && (shadow_off & 15) == 0 &&
-                      ((ldw * 2) & 15) == 0;
-    uint8_t* const stage = &s.epi_stage[0][0];
-    static_assert(4 * kEpiStageBytes >= 2 * U * 2 * 512, "pass buffers exceed the staging area");
-    const int npass = (total + U * c.nthr - 1) / (U * c.nthr);
-    for (int pass = 0; pass < npass; ++pass) {
-      const int e0 = c.tid + pass * U * c.nthr;
-      uint8_t* const buf = stage + (pass & 1) * (U * 2 * 512);
-      if (bulk && pass >= 2) {
-        if (c.et == 0) bulk_wait_read<1>();  // pass-2's copies have read this buffer
-        epi_sync();
-      }
+    for (int e0 = c.tid; e0 < total; e0 += U * c.nthr) {
       float4 gs[U], wv[U];
       int soff[U];
       long long idx[U];
@@ -1433,35 +1419,9 @@ __device__ void op_dp_reduce(const KParams& p, SmemT<P>& s, const EpiCtx& c, con
         w.w = fmaf(-lr, gs[u].w, wv[u].w);
         *reinterpret_cast<float4*>(d.w_out + idx[u]) = w;
         const uint2 pk = make_uint2(pack_bf16x2(w.x, w.y), pack_bf16x2(w.z, w.w));
-        if (bulk) {
-          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(own + shadow_off) + idx[u]) = pk;
-          *reinterpret_cast<uint2*>(buf + (u * 2 + (c.et >> 6)) * 512 + (c.et & 63) * 8) = pk;
-        } else {
-          for (int r2 = 0; r2 < dp->world; ++r2)
-            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + idx[u]) = pk;
-        }
+        for (int r2 = 0; r2 < dp->world; ++r2)
+          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + idx[u]) = pk;
       }
-      if (bulk) {
-        fence_proxy_async_smem();
-        epi_sync();
-        if (c.et == 0) {
-          for (int u = 0; u < U; ++u)
-            for (int h = 0; h < 2; ++h) {
-              const int er = pass * U * c.nthr + u * c.nthr + int(c.rank) * kEpiThreads + h * 64;
-              if (er >= total) continue;
-              const long long ridx = (long long)(row0 + er / cg) * ldw + n0;
-              for (int r2 = 0; r2 < dp->world; ++r2)
-                if (r2 != dp->rank)
-                  bulk_store_1d(reinterpret_cast<uint16_t*>(dp->base[r2] + shadow_off) + ridx,
-                                buf + (u * 2 + h) * 512, 512);
-            }
-          bulk_commit();
-        }
-      }
-    }
-    if (bulk && c.et == 0) {
-      bulk_wait_all();  // the copies have landed in the peers' memory
-      fence_proxy_async_global();
     }
   } else {
     for (int e = c.tid; e < total; e += c.nthr) {
@@ -1643,7 +1603,7 @@ __device__ void compute_loop(const KParams& p, SmemT<P>& s, uint32_t tmem_base, 
         op_dp_bias_send(p, c, *reinterpret_cast<const pkt_dp_bias_args*>(task.args));
         break;
       case PKT_OP_DP_REDUCE:
-        op_dp_reduce<P>(p, s, c, *reinterpret_cast<const pkt_gemm_tile_args*>(task.args));
+        op_dp_reduce<P>(p, s, c, *reinterpret_cast<const pkt_gemm_tile_args*>(task.args), tr);
         break;
       case PKT_OP_DP_BIAS_APPLY:
         op_dp_bias_apply(p, c, *reinterpret_cast<const pkt_dp_bias_args*>(task.args));

@@ -101,13 +101,6 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_
       "r"(smem_u32(smem_src)), "r"(x), "r"(y)
       : "memory");
 }
-// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
-// shared memory to global memory (this GPU's or a peer's), in the current bulk group.
-__device__ __forceinline__ void bulk_store_1d(void* gdst, const void* smem_src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
-               "r"(smem_u32(smem_src)), "r"(bytes)
-               : "memory");
-}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // This thread's bulk stores have finished reading their shared-memory source.
 __device__ __forceinline__ void bulk_wait_read_all() {
